@@ -1,0 +1,176 @@
+"""ctypes binding of libfgw_mha.so (the C ABI declared in include/fgw_mha.h).
+
+The library is loaded from ``fgw_b200/_lib`` (built in-tree by ``python -m fgw_b200.build``).
+There is no fallback: if the library is missing or cannot be loaded, every entry point raises
+``NativeLibraryError`` naming the file, so a GPU box without the built extension fails loudly.
+"""
+import ctypes
+import pathlib
+
+LIB_PATH = pathlib.Path(__file__).resolve().parent / "_lib" / "libfgw_mha.so"
+
+# fgw_status codes
+OK = 0
+ERR_INVALID_ARGUMENT = 1
+ERR_UNSUPPORTED = 2
+ERR_WORKSPACE_TOO_SMALL = 3
+ERR_CUDA = 4
+ERR_DEVICE_TIMEOUT = 5
+ERR_NO_DEVICE = 6
+
+DTYPE_FLOAT16 = 0
+DTYPE_BFLOAT16 = 1
+
+PATH_AUTO = 0
+PATH_DECODE = 1
+PATH_TENSOR = 2
+
+EXPORTED = (
+    "fgw_mha_abi_version",
+    "fgw_mha_status_string",
+    "fgw_mha_device_sm_count",
+    "fgw_mha_resolve_path",
+    "fgw_mha_workspace_size",
+    "fgw_mha_paged_fwd",
+    "fgw_mha_partial",
+    "fgw_mha_merge",
+    "fgw_mha_read_error",
+)
+
+
+class NativeLibraryError(RuntimeError):
+    """libfgw_mha.so is absent or unusable."""
+
+
+class FgwError(RuntimeError):
+    """A C-ABI call returned a non-zero fgw_status."""
+
+    def __init__(self, status, where):
+        self.status = status
+        super().__init__(f"{where}: {status_string(status)} (fgw_status {status})")
+
+
+class Params(ctypes.Structure):
+    """Mirror of ``fgw_mha_params`` (include/fgw_mha.h)."""
+
+    _fields_ = [
+        ("q", ctypes.c_void_p),
+        ("k_cache", ctypes.c_void_p),
+        ("v_cache", ctypes.c_void_p),
+        ("block_table", ctypes.c_void_p),
+        ("cache_seqlens", ctypes.c_void_p),
+        ("out", ctypes.c_void_p),
+        ("pool_rows", ctypes.c_int64),
+        ("batch", ctypes.c_int32),
+        ("q_len", ctypes.c_int32),
+        ("heads", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32),
+        ("table_width", ctypes.c_int32),
+        ("page_size", ctypes.c_int32),
+        ("dtype", ctypes.c_int32),
+        ("causal", ctypes.c_int32),
+        ("num_splits", ctypes.c_int32),
+        ("grid_cap", ctypes.c_int32),
+        ("path", ctypes.c_int32),
+        ("wait_budget_ms", ctypes.c_int32),
+        ("reserved", ctypes.c_int32 * 4),
+    ]
+
+
+_LIB = None
+
+
+def library():
+    """The loaded ``ctypes.CDLL``; raises ``NativeLibraryError`` if it cannot be loaded."""
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    if not LIB_PATH.exists():
+        raise NativeLibraryError(
+            f"{LIB_PATH} is missing: build it with `python -m fgw_b200.build` (nvcc 12.9, sm_100a). "
+            "There is no CPU fallback for the paged MHA forward.")
+    try:
+        lib = ctypes.CDLL(str(LIB_PATH))
+    except OSError as exc:
+        raise NativeLibraryError(f"cannot load {LIB_PATH}: {exc}") from exc
+    missing = [name for name in EXPORTED if not hasattr(lib, name)]
+    if missing:
+        raise NativeLibraryError(f"{LIB_PATH} lacks exported symbols {missing}")
+    p = ctypes.POINTER(Params)
+    vp = ctypes.c_void_p
+    lib.fgw_mha_abi_version.argtypes = []
+    lib.fgw_mha_abi_version.restype = ctypes.c_int
+    lib.fgw_mha_status_string.argtypes = [ctypes.c_int]
+    lib.fgw_mha_status_string.restype = ctypes.c_char_p
+    lib.fgw_mha_device_sm_count.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_int)]
+    lib.fgw_mha_device_sm_count.restype = ctypes.c_int
+    lib.fgw_mha_resolve_path.argtypes = [p, ctypes.POINTER(ctypes.c_int)]
+    lib.fgw_mha_resolve_path.restype = ctypes.c_int
+    lib.fgw_mha_workspace_size.argtypes = [p, ctypes.POINTER(ctypes.c_size_t)]
+    lib.fgw_mha_workspace_size.restype = ctypes.c_int
+    for name in ("fgw_mha_paged_fwd", "fgw_mha_partial", "fgw_mha_merge"):
+        fn = getattr(lib, name)
+        fn.argtypes = [p, vp, ctypes.c_size_t, vp]
+        fn.restype = ctypes.c_int
+    lib.fgw_mha_read_error.argtypes = [vp, vp, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int)]
+    lib.fgw_mha_read_error.restype = ctypes.c_int
+    _LIB = lib
+    return lib
+
+
+def status_string(status):
+    try:
+        return library().fgw_mha_status_string(int(status)).decode()
+    except NativeLibraryError:
+        return f"status {status}"
+
+
+def check(status, where):
+    if status != OK:
+        raise FgwError(status, where)
+
+
+def abi_version():
+    return library().fgw_mha_abi_version()
+
+
+def device_sm_count(device):
+    out = ctypes.c_int(0)
+    check(library().fgw_mha_device_sm_count(int(device), ctypes.byref(out)), "fgw_mha_device_sm_count")
+    return out.value
+
+
+def resolve_path(params):
+    out = ctypes.c_int(0)
+    check(library().fgw_mha_resolve_path(ctypes.byref(params), ctypes.byref(out)), "fgw_mha_resolve_path")
+    return out.value
+
+
+def workspace_size(params):
+    out = ctypes.c_size_t(0)
+    check(library().fgw_mha_workspace_size(ctypes.byref(params), ctypes.byref(out)), "fgw_mha_workspace_size")
+    return out.value
+
+
+def paged_fwd(params, workspace_ptr, workspace_bytes, stream_ptr):
+    check(library().fgw_mha_paged_fwd(ctypes.byref(params), workspace_ptr, workspace_bytes, stream_ptr),
+          "fgw_mha_paged_fwd")
+
+
+def partial(params, workspace_ptr, workspace_bytes, stream_ptr):
+    check(library().fgw_mha_partial(ctypes.byref(params), workspace_ptr, workspace_bytes, stream_ptr),
+          "fgw_mha_partial")
+
+
+def merge(params, workspace_ptr, workspace_bytes, stream_ptr):
+    check(library().fgw_mha_merge(ctypes.byref(params), workspace_ptr, workspace_bytes, stream_ptr),
+          "fgw_mha_merge")
+
+
+def read_error(workspace_ptr, stream_ptr):
+    """(device_status, site) recorded in the workspace header; synchronises the stream."""
+    status = ctypes.c_int(0)
+    site = ctypes.c_int(0)
+    check(library().fgw_mha_read_error(workspace_ptr, stream_ptr, ctypes.byref(status), ctypes.byref(site)),
+          "fgw_mha_read_error")
+    return status.value, site.value

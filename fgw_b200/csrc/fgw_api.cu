@@ -1,0 +1,223 @@
+// C ABI of libfgw_mha.so: argument validation, workspace carve-up, path choice and launch order.
+// The host-side control flow mirrors the reference's launch callables (v7.py:471-498,
+// cube_general.py:186-188, 284-288): one launch when there is one split, partial then merge
+// otherwise, all on the caller's stream. A small planning launch precedes them and replaces the
+// reference's host copy of the cache lengths (v7.py:548).
+#include <cstring>
+#include <mutex>
+
+#include "fgw_common.cuh"
+#include "fgw_kernels.h"
+
+namespace fgw {
+
+static size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+    }
+  });
+  return fn;
+}
+
+size_t workspace_bytes(const fgw_mha_params& p, int /*path*/) {
+  size_t bytes = sizeof(WorkspaceHeader);
+  bytes += align256(sizeof(int32_t) * p.batch);  // lens
+  bytes += align256(sizeof(int32_t) * p.batch);  // order
+  const size_t rows = static_cast<size_t>(p.batch) * p.q_len * p.heads;
+  if (p.num_splits > 1) {
+    bytes += align256(rows * p.num_splits * sizeof(float));
+    bytes += align256(rows * p.num_splits * p.head_dim * sizeof(float));
+  }
+  return bytes;
+}
+
+void carve_workspace(LaunchDesc& d, void* workspace, int /*path*/) {
+  const fgw_mha_params& p = d.p;
+  uint8_t* base = static_cast<uint8_t*>(workspace);
+  d.header = reinterpret_cast<WorkspaceHeader*>(base);
+  base += sizeof(WorkspaceHeader);
+  d.lens = reinterpret_cast<int32_t*>(base);
+  base += align256(sizeof(int32_t) * p.batch);
+  d.order = reinterpret_cast<int32_t*>(base);
+  base += align256(sizeof(int32_t) * p.batch);
+  const size_t rows = static_cast<size_t>(p.batch) * p.q_len * p.heads;
+  d.part_lse = reinterpret_cast<float*>(base);
+  base += align256(rows * p.num_splits * sizeof(float));
+  d.part_o = reinterpret_cast<float*>(base);
+}
+
+int resolve_path(const fgw_mha_params& p) {
+  if (p.path == FGW_PATH_DECODE || p.path == FGW_PATH_TENSOR) return p.path;
+  return FGW_PATH_DECODE;
+}
+
+static bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
+
+static int validate(const fgw_mha_params* p) {
+  if (p == nullptr) return FGW_ERR_INVALID_ARGUMENT;
+  if (p->batch <= 0 || p->q_len <= 0 || p->heads <= 0 || p->head_dim <= 0) return FGW_ERR_INVALID_ARGUMENT;
+  if (p->head_dim < 16 || p->head_dim > 256 || p->head_dim % 16) return FGW_ERR_INVALID_ARGUMENT;
+  if (p->page_size <= 0 || p->page_size % 16) return FGW_ERR_INVALID_ARGUMENT;
+  if (p->pool_rows <= 0 || p->pool_rows % p->page_size || p->pool_rows >= (1ll << 31)) {
+    return FGW_ERR_INVALID_ARGUMENT;
+  }
+  if (p->table_width <= 0) return FGW_ERR_INVALID_ARGUMENT;
+  if (static_cast<long long>(p->table_width) * p->page_size >= (1ll << 31)) return FGW_ERR_INVALID_ARGUMENT;
+  if (p->dtype != FGW_DTYPE_FLOAT16 && p->dtype != FGW_DTYPE_BFLOAT16) return FGW_ERR_INVALID_ARGUMENT;
+  if (p->causal != 0 && p->causal != 1) return FGW_ERR_INVALID_ARGUMENT;
+  if (p->num_splits < 1 || p->num_splits > 1024) return FGW_ERR_INVALID_ARGUMENT;
+  if (p->grid_cap < 0 || p->wait_budget_ms < 0) return FGW_ERR_INVALID_ARGUMENT;
+  if (p->path < FGW_PATH_AUTO || p->path > FGW_PATH_TENSOR) return FGW_ERR_INVALID_ARGUMENT;
+  for (int i = 0; i < 4; ++i) {
+    if (p->reserved[i] != 0) return FGW_ERR_INVALID_ARGUMENT;
+  }
+  if (!p->q || !p->k_cache || !p->v_cache || !p->block_table || !p->cache_seqlens || !p->out) {
+    return FGW_ERR_INVALID_ARGUMENT;
+  }
+  if (!aligned16(p->q) || !aligned16(p->k_cache) || !aligned16(p->v_cache) || !aligned16(p->out) ||
+      (reinterpret_cast<uintptr_t>(p->block_table) & 3u) || (reinterpret_cast<uintptr_t>(p->cache_seqlens) & 3u)) {
+    return FGW_ERR_INVALID_ARGUMENT;
+  }
+  return FGW_OK;
+}
+
+static int device_sm_count_cached(int device, int* sms) {
+  static std::mutex mu;
+  static int cache[64] = {0};
+  if (device < 0 || device >= 64) return FGW_ERR_NO_DEVICE;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache[device] == 0) {
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) return FGW_ERR_NO_DEVICE;
+    if (prop.major != 10) return FGW_ERR_NO_DEVICE;
+    cache[device] = prop.multiProcessorCount;
+  }
+  *sms = cache[device];
+  return FGW_OK;
+}
+
+static int prepare(const fgw_mha_params* params, void* workspace, size_t workspace_bytes_given, void* stream,
+                   LaunchDesc& d) {
+  int st = validate(params);
+  if (st != FGW_OK) return st;
+  if (workspace == nullptr || (reinterpret_cast<uintptr_t>(workspace) & 255u)) return FGW_ERR_INVALID_ARGUMENT;
+  std::memset(&d, 0, sizeof(d));
+  d.p = *params;
+  const int path = resolve_path(d.p);
+  if (workspace_bytes_given < workspace_bytes(d.p, path)) return FGW_ERR_WORKSPACE_TOO_SMALL;
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess) return FGW_ERR_NO_DEVICE;
+  st = device_sm_count_cached(device, &d.sm_count);
+  if (st != FGW_OK) return st;
+  if (encode_tiled() == nullptr) return FGW_ERR_CUDA;
+  carve_workspace(d, workspace, path);
+  const int budget_ms = d.p.wait_budget_ms > 0 ? d.p.wait_budget_ms : 2000;
+  d.budget_ns = static_cast<uint64_t>(budget_ms) * 1000000ull;
+  d.stream = static_cast<cudaStream_t>(stream);
+  return FGW_OK;
+}
+
+static int launch_main(const LaunchDesc& d, bool partials) {
+  const int path = resolve_path(d.p);
+  cudaError_t err = path == FGW_PATH_TENSOR ? launch_tensor(d, partials) : launch_decode(d, partials);
+  if (err == cudaErrorNotSupported) return FGW_ERR_UNSUPPORTED;
+  return err == cudaSuccess ? FGW_OK : FGW_ERR_CUDA;
+}
+
+}  // namespace fgw
+
+using namespace fgw;
+
+extern "C" {
+
+int fgw_mha_abi_version(void) { return FGW_MHA_ABI_VERSION; }
+
+const char* fgw_mha_status_string(int status) {
+  switch (status) {
+    case FGW_OK:
+      return "ok";
+    case FGW_ERR_INVALID_ARGUMENT:
+      return "invalid argument";
+    case FGW_ERR_UNSUPPORTED:
+      return "unsupported configuration";
+    case FGW_ERR_WORKSPACE_TOO_SMALL:
+      return "workspace too small";
+    case FGW_ERR_CUDA:
+      return "CUDA error";
+    case FGW_ERR_DEVICE_TIMEOUT:
+      return "device-side wait timed out";
+    case FGW_ERR_NO_DEVICE:
+      return "no sm_100 device";
+    default:
+      return "unknown status";
+  }
+}
+
+int fgw_mha_device_sm_count(int device, int* sm_count) {
+  if (sm_count == nullptr) return FGW_ERR_INVALID_ARGUMENT;
+  return device_sm_count_cached(device, sm_count);
+}
+
+int fgw_mha_resolve_path(const fgw_mha_params* params, int* path) {
+  if (params == nullptr || path == nullptr) return FGW_ERR_INVALID_ARGUMENT;
+  *path = resolve_path(*params);
+  return FGW_OK;
+}
+
+int fgw_mha_workspace_size(const fgw_mha_params* params, size_t* bytes) {
+  if (params == nullptr || bytes == nullptr) return FGW_ERR_INVALID_ARGUMENT;
+  fgw_mha_params p = *params;
+  if (p.batch <= 0 || p.q_len <= 0 || p.heads <= 0 || p.head_dim <= 0 || p.num_splits < 1) {
+    return FGW_ERR_INVALID_ARGUMENT;
+  }
+  *bytes = workspace_bytes(p, resolve_path(p));
+  return FGW_OK;
+}
+
+int fgw_mha_paged_fwd(const fgw_mha_params* params, void* workspace, size_t workspace_bytes_given, void* stream) {
+  LaunchDesc d;
+  int st = prepare(params, workspace, workspace_bytes_given, stream, d);
+  if (st != FGW_OK) return st;
+  if (launch_plan(d) != cudaSuccess) return FGW_ERR_CUDA;
+  const bool split = d.p.num_splits > 1;
+  st = launch_main(d, split);
+  if (st != FGW_OK) return st;
+  if (split && launch_merge(d) != cudaSuccess) return FGW_ERR_CUDA;
+  return FGW_OK;
+}
+
+int fgw_mha_partial(const fgw_mha_params* params, void* workspace, size_t workspace_bytes_given, void* stream) {
+  LaunchDesc d;
+  int st = prepare(params, workspace, workspace_bytes_given, stream, d);
+  if (st != FGW_OK) return st;
+  if (d.p.num_splits < 2) return FGW_ERR_INVALID_ARGUMENT;
+  if (launch_plan(d) != cudaSuccess) return FGW_ERR_CUDA;
+  return launch_main(d, true);
+}
+
+int fgw_mha_merge(const fgw_mha_params* params, void* workspace, size_t workspace_bytes_given, void* stream) {
+  LaunchDesc d;
+  int st = prepare(params, workspace, workspace_bytes_given, stream, d);
+  if (st != FGW_OK) return st;
+  return launch_merge(d) == cudaSuccess ? FGW_OK : FGW_ERR_CUDA;
+}
+
+int fgw_mha_read_error(const void* workspace, void* stream, int* device_status, int* site) {
+  if (workspace == nullptr || device_status == nullptr) return FGW_ERR_INVALID_ARGUMENT;
+  if (cudaStreamSynchronize(static_cast<cudaStream_t>(stream)) != cudaSuccess) return FGW_ERR_CUDA;
+  int32_t words[2] = {0, 0};
+  if (cudaMemcpy(words, workspace, sizeof(words), cudaMemcpyDeviceToHost) != cudaSuccess) return FGW_ERR_CUDA;
+  *device_status = words[0];
+  if (site != nullptr) *site = words[1];
+  return FGW_OK;
+}
+
+}  // extern "C"

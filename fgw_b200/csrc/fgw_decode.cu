@@ -1,0 +1,480 @@
+// Warp-level, HBM-streaming paged attention for short query blocks (decode, q_len ~ 1).
+//
+// Replaces the reference's SIMT split-KV kernels (operators/mha/kernels/mha_paged_decode_ascend_v2.py:34-129,
+// v1 for one split) and the Q~1 use of the v7 Cube kernel. Design for B200:
+//   * one persistent CTA per SM walks a static round-robin list of work items
+//     (request, query-row block, split, head) in descending-cache-length order (LPT);
+//   * a producer warp streams each item's live KV pages into a shared-memory ring with TMA,
+//     one 3-D box {head_dim, 1, rows} per (page slice, K or V), driven by the block table;
+//   * eight consumer warps split a tile's tokens into groups of LPT lanes; each group owns
+//     whole tokens, reduces q.k across its lanes with shuffles and keeps an online-softmax
+//     state (max, sum, accumulator) in base 2;
+//   * states are merged across groups (shuffles) and warps (shared memory) at the end of the item,
+//     which writes the final output (one split) or an FP32 partial plus base-2 LSE.
+// Masked tokens never touch the accumulator, so NaN-filled rows past a cache's end cannot leak
+// (0 * NaN would): the reference relies on the same guard (v2.py:107-109, cube_general.py:93-109).
+#include <algorithm>
+
+#include "fgw_common.cuh"
+#include "fgw_kernels.h"
+
+namespace fgw {
+
+struct DecodeArgs {
+  const void* q;
+  void* out;
+  const int32_t* table;
+  const int32_t* lengths;
+  const int32_t* order;
+  float* part_o;
+  float* part_lse;
+  WorkspaceHeader* ws;
+  int batch, sq, heads, width, page, splits, causal, row_blocks, box_rows, write_partials;
+  long long items;
+  float scale_log2;
+  uint64_t budget_ns;
+};
+
+template <int D>
+struct DecodeShape {
+  static constexpr int kChunks = D / 8;                    // 16-byte chunks per row
+  static constexpr int kLpt = kChunks >= 8 ? 8 : (kChunks >= 4 ? 4 : 2);  // lanes per token
+  static constexpr int kCpl = (kChunks + kLpt - 1) / kLpt;  // chunks per lane
+  static constexpr int kGpw = 32 / kLpt;                   // token groups per warp
+  static constexpr int kWarps = 8;                         // consumer warps
+  static constexpr int kGroups = kWarps * kGpw;
+  static constexpr int kTile = kGroups > 64 ? kGroups : 64;  // tokens per pipeline stage
+  static constexpr int kTpg = kTile / kGroups;             // tokens per group per tile
+  static constexpr int kRows = (kCpl * 8 >= 32) ? 1 : ((kCpl * 8 >= 16) ? 2 : 4);  // query rows per item
+  static constexpr int kThreads = (kWarps + 1) * 32;
+};
+
+template <typename T, int D>
+struct DecodeSmem {
+  using S = DecodeShape<D>;
+  static constexpr int kStageBytes = 2 * S::kTile * D * (int)sizeof(T);
+  static constexpr int kStages = std::min(8, std::max(2, (160 * 1024) / kStageBytes));
+  static constexpr int kRedFloats = S::kWarps * S::kRows * (D + 2);
+  static constexpr int kBytes = kStages * kStageBytes + 2 * kStages * 8 + kRedFloats * 4 + 64;
+};
+
+__device__ __forceinline__ void decode_item(long long item, int heads, int splits, int row_blocks,
+                                            const int32_t* order, int& b, int& rb, int& s, int& h) {
+  h = static_cast<int>(item % heads);
+  long long rest = item / heads;
+  s = static_cast<int>(rest % splits);
+  rest /= splits;
+  rb = static_cast<int>(rest % row_blocks);
+  b = order[rest / row_blocks];
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(DecodeShape<D>::kThreads, 1)
+    decode_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
+                  const DecodeArgs a) {
+  using S = DecodeShape<D>;
+  using M = DecodeSmem<T, D>;
+  using Tr = ElemTraits<T>;
+  constexpr int kRows = S::kRows;
+  constexpr int kStages = M::kStages;
+
+  extern __shared__ __align__(128) uint8_t smem[];
+  T* ring = reinterpret_cast<T*>(smem);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * M::kStageBytes);
+  uint64_t* empty = full + kStages;
+  float* red = reinterpret_cast<float*>(empty + kStages);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], S::kWarps);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  const int grid = gridDim.x;
+  if (warp == S::kWarps) {
+    // ----------------------------------------------------------------- producer warp
+    if (lane == 0) {
+      tma_prefetch_desc(&kmap);
+      tma_prefetch_desc(&vmap);
+      const uint64_t policy = l2_policy_evict_first();
+      bool ok = true;
+      uint32_t it = 0;
+      const int boxes = S::kTile / a.box_rows;
+      const uint32_t box_bytes = a.box_rows * D * sizeof(T);
+      for (long long item = blockIdx.x; item < a.items; item += grid) {
+        int b, rb, s, h;
+        decode_item(item, a.heads, a.splits, a.row_blocks, a.order, b, rb, s, h);
+        const int len = a.lengths[b];
+        const int last_row = min(rb * kRows + kRows, a.sq) - 1;
+        const int end_tok = a.causal ? max(len - a.sq + last_row + 1, 0) : len;
+        const int tiles = (end_tok + S::kTile - 1) / S::kTile;
+        const int t_begin = (int)((long long)tiles * s / a.splits);
+        const int t_end = (int)((long long)tiles * (s + 1) / a.splits);
+        const int32_t* row_table = a.table + (long long)b * a.width;
+        for (int t = t_begin; t < t_end; ++t, ++it) {
+          const int stage = it % kStages;
+          const uint32_t phase = (it / kStages) & 1;
+          if (ok && !mbar_wait(&empty[stage], phase ^ 1, a.budget_ns)) {
+            ok = false;
+            record_error(a.ws, FGW_ERR_DEVICE_TIMEOUT, 1);
+          }
+          if (!ok) continue;
+          const int tok0 = t * S::kTile;
+          int nb = 0;
+          for (int k = 0; k < boxes; ++k) nb += (tok0 + k * a.box_rows < end_tok) ? 1 : 0;
+          mbar_arrive_expect_tx(&full[stage], 2u * nb * box_bytes);
+          T* kdst = ring + (size_t)stage * (2 * S::kTile * D);
+          T* vdst = kdst + S::kTile * D;
+          for (int k = 0; k < nb; ++k) {
+            const int tok = tok0 + k * a.box_rows;
+            const int row = row_table[tok / a.page] * a.page + tok % a.page;
+            tma_load_3d_hint(kdst + k * a.box_rows * D, &kmap, &full[stage], 0, h, row, policy);
+            tma_load_3d_hint(vdst + k * a.box_rows * D, &vmap, &full[stage], 0, h, row, policy);
+          }
+        }
+      }
+      // Leave no copy in flight: wait for the stages still owed to the consumers.
+      if (!ok) {
+        for (uint32_t j = 0; j < (uint32_t)kStages && j < it; ++j) {
+          const uint32_t k = it - 1 - j;
+          mbar_wait(&full[k % kStages], (k / kStages) & 1, a.budget_ns);
+        }
+      }
+    }
+    return;
+  }
+
+  // ------------------------------------------------------------------- consumer warps
+  const int group_in_warp = lane / S::kLpt;
+  const int lane_in_group = lane % S::kLpt;
+  const int group = warp * S::kGpw + group_in_warp;
+  const uint32_t group_mask = (S::kLpt == 32 ? 0xffffffffu : ((1u << S::kLpt) - 1u)) << (group_in_warp * S::kLpt);
+  const uint32_t consumer_threads = S::kWarps * 32;
+  bool ok = true;
+  uint32_t it = 0;
+
+  for (long long item = blockIdx.x; item < a.items; item += grid) {
+    int b, rb, s, h;
+    decode_item(item, a.heads, a.splits, a.row_blocks, a.order, b, rb, s, h);
+    const int len = a.lengths[b];
+    const int q0 = rb * kRows;
+    int vis[kRows];
+    int end_tok = 0;
+#pragma unroll
+    for (int r = 0; r < kRows; ++r) {
+      const int qi = q0 + r;
+      vis[r] = qi < a.sq ? (a.causal ? max(len - a.sq + qi + 1, 0) : len) : 0;
+      end_tok = max(end_tok, vis[r]);
+    }
+    const int tiles = (end_tok + S::kTile - 1) / S::kTile;
+    const int t_begin = (int)((long long)tiles * s / a.splits);
+    const int t_end = (int)((long long)tiles * (s + 1) / a.splits);
+
+    // Query rows for this lane's chunks, pre-scaled into the base-2 score domain.
+    float qv[kRows][S::kCpl * 8];
+#pragma unroll
+    for (int r = 0; r < kRows; ++r) {
+      const int qi = min(q0 + r, a.sq - 1);
+      const T* qrow = reinterpret_cast<const T*>(a.q) + (((long long)b * a.sq + qi) * a.heads + h) * D;
+#pragma unroll
+      for (int c = 0; c < S::kCpl; ++c) {
+        const int ci = lane_in_group + c * S::kLpt;
+        uint4 raw = make_uint4(0, 0, 0, 0);
+        if (ci < S::kChunks) raw = *reinterpret_cast<const uint4*>(qrow + ci * 8);
+        const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = Tr::unpack2(w[e]);
+          qv[r][c * 8 + 2 * e] = f.x * a.scale_log2;
+          qv[r][c * 8 + 2 * e + 1] = f.y * a.scale_log2;
+        }
+      }
+    }
+    float m[kRows], l[kRows], acc[kRows][S::kCpl * 8];
+#pragma unroll
+    for (int r = 0; r < kRows; ++r) {
+      m[r] = -INFINITY;
+      l[r] = 0.f;
+#pragma unroll
+      for (int e = 0; e < S::kCpl * 8; ++e) acc[r][e] = 0.f;
+    }
+
+    for (int t = t_begin; t < t_end; ++t, ++it) {
+      const int stage = it % kStages;
+      const uint32_t phase = (it / kStages) & 1;
+      if (ok) {
+        // Keep `ok` warp-uniform: the group shuffles below need every lane of the group.
+        ok = __all_sync(0xffffffffu, mbar_wait(&full[stage], phase, a.budget_ns));
+        if (!ok && lane == 0) record_error(a.ws, FGW_ERR_DEVICE_TIMEOUT, 2);
+      }
+      if (ok) {
+        const T* ktile = ring + (size_t)stage * (2 * S::kTile * D);
+        const T* vtile = ktile + S::kTile * D;
+        const int tok0 = t * S::kTile;
+#pragma unroll 1
+        for (int j = 0; j < S::kTpg; ++j) {
+          const int tt = group + j * S::kGroups;
+          const int tok = tok0 + tt;
+          if (tok >= end_tok) break;  // uniform within the group
+          float kf[S::kCpl * 8];
+#pragma unroll
+          for (int c = 0; c < S::kCpl; ++c) {
+            const int ci = lane_in_group + c * S::kLpt;
+            uint4 raw = make_uint4(0, 0, 0, 0);
+            if (ci < S::kChunks) raw = *reinterpret_cast<const uint4*>(ktile + tt * D + ci * 8);
+            const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 f = Tr::unpack2(w[e]);
+              kf[c * 8 + 2 * e] = f.x;
+              kf[c * 8 + 2 * e + 1] = f.y;
+            }
+          }
+          float sc[kRows];
+#pragma unroll
+          for (int r = 0; r < kRows; ++r) {
+            float dot = 0.f;
+#pragma unroll
+            for (int e = 0; e < S::kCpl * 8; ++e) dot = fmaf(qv[r][e], kf[e], dot);
+            // Only this group's lanes take part: groups leave the token loop independently.
+#pragma unroll
+            for (int off = S::kLpt / 2; off > 0; off >>= 1) dot += __shfl_xor_sync(group_mask, dot, off);
+            sc[r] = dot;
+          }
+          float vf[S::kCpl * 8];
+#pragma unroll
+          for (int c = 0; c < S::kCpl; ++c) {
+            const int ci = lane_in_group + c * S::kLpt;
+            uint4 raw = make_uint4(0, 0, 0, 0);
+            if (ci < S::kChunks) raw = *reinterpret_cast<const uint4*>(vtile + tt * D + ci * 8);
+            const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 f = Tr::unpack2(w[e]);
+              vf[c * 8 + 2 * e] = f.x;
+              vf[c * 8 + 2 * e + 1] = f.y;
+            }
+          }
+#pragma unroll
+          for (int r = 0; r < kRows; ++r) {
+            if (tok < vis[r]) {
+              if (sc[r] > m[r]) {
+                const float corr = fast_exp2(m[r] - sc[r]);  // exp2(-inf) = 0 on the first key
+                l[r] *= corr;
+#pragma unroll
+                for (int e = 0; e < S::kCpl * 8; ++e) acc[r][e] *= corr;
+                m[r] = sc[r];
+              }
+              const float pr = fast_exp2(sc[r] - m[r]);
+              l[r] += pr;
+#pragma unroll
+              for (int e = 0; e < S::kCpl * 8; ++e) acc[r][e] = fmaf(pr, vf[e], acc[r][e]);
+            }
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[stage]);
+    }
+
+    // Merge group states inside the warp (groups differ in the high lane bits).
+#pragma unroll
+    for (int r = 0; r < kRows; ++r) {
+#pragma unroll
+      for (int off = S::kLpt; off < 32; off <<= 1) {
+        const float mo = __shfl_xor_sync(0xffffffffu, m[r], off);
+        const float lo = __shfl_xor_sync(0xffffffffu, l[r], off);
+        const float mn = fmaxf(m[r], mo);
+        const float ca = (m[r] == -INFINITY) ? 0.f : fast_exp2(m[r] - mn);
+        const float cb = (mo == -INFINITY) ? 0.f : fast_exp2(mo - mn);
+        l[r] = l[r] * ca + lo * cb;
+#pragma unroll
+        for (int e = 0; e < S::kCpl * 8; ++e) {
+          const float ao = __shfl_xor_sync(0xffffffffu, acc[r][e], off);
+          acc[r][e] = acc[r][e] * ca + ao * cb;
+        }
+        m[r] = mn;
+      }
+    }
+    // Group 0 of each warp publishes the warp state: red[warp][row][0..D) acc, [D] max, [D+1] sum.
+    if (group_in_warp == 0) {
+#pragma unroll
+      for (int r = 0; r < kRows; ++r) {
+        float* dst = red + (warp * kRows + r) * (D + 2);
+#pragma unroll
+        for (int c = 0; c < S::kCpl; ++c) {
+          const int ci = lane_in_group + c * S::kLpt;
+          if (ci < S::kChunks) {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) dst[ci * 8 + e] = acc[r][c * 8 + e];
+          }
+        }
+        if (lane_in_group == 0) {
+          dst[D] = m[r];
+          dst[D + 1] = l[r];
+        }
+      }
+    }
+    named_barrier_sync(1, consumer_threads);
+    for (int idx = threadIdx.x; idx < kRows * D; idx += consumer_threads) {
+      const int r = idx / D;
+      const int d = idx % D;
+      const int qi = q0 + r;
+      if (qi >= a.sq) continue;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < S::kWarps; ++w) mx = fmaxf(mx, red[(w * kRows + r) * (D + 2) + D]);
+      float num = 0.f, den = 0.f;
+      if (mx != -INFINITY) {
+#pragma unroll
+        for (int w = 0; w < S::kWarps; ++w) {
+          const float* src = red + (w * kRows + r) * (D + 2);
+          const float mw = src[D];
+          const float f = (mw == -INFINITY) ? 0.f : fast_exp2(mw - mx);
+          num = fmaf(src[d], f, num);
+          den = fmaf(src[D + 1], f, den);
+        }
+      }
+      const long long row_id = ((long long)b * a.sq + qi) * a.heads + h;
+      const float val = den > 0.f ? num / den : 0.f;
+      if (a.write_partials) {
+        a.part_o[(row_id * a.splits + s) * D + d] = val;
+        if (d == 0) a.part_lse[row_id * a.splits + s] = den > 0.f ? mx + fast_log2(den) : kEmptyLse;
+      } else {
+        reinterpret_cast<T*>(a.out)[row_id * D + d] = Tr::from_float(val);
+      }
+    }
+    named_barrier_sync(1, consumer_threads);
+  }
+}
+
+template <typename T, int D>
+static cudaError_t launch_decode_t(const LaunchDesc& d, const DecodeArgs& args, const CUtensorMap& kmap,
+                                   const CUtensorMap& vmap) {
+  using S = DecodeShape<D>;
+  using M = DecodeSmem<T, D>;
+  auto kernel = decode_kernel<T, D>;
+  cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, M::kBytes);
+  if (err != cudaSuccess) return err;
+  long long grid = args.items;
+  const long long cap = d.p.grid_cap > 0 ? d.p.grid_cap : d.sm_count;
+  grid = std::min(grid, cap);
+  if (grid <= 0) return cudaSuccess;
+  kernel<<<(unsigned)grid, S::kThreads, M::kBytes, d.stream>>>(kmap, vmap, args);
+  return cudaGetLastError();
+}
+
+int decode_rows_per_item(int head_dim) {
+  switch (head_dim) {
+#define FGW_ROWS_CASE(DD) \
+  case DD:                \
+    return DecodeShape<DD>::kRows;
+    FGW_ROWS_CASE(16)
+    FGW_ROWS_CASE(32)
+    FGW_ROWS_CASE(48)
+    FGW_ROWS_CASE(64)
+    FGW_ROWS_CASE(80)
+    FGW_ROWS_CASE(96)
+    FGW_ROWS_CASE(112)
+    FGW_ROWS_CASE(128)
+    FGW_ROWS_CASE(144)
+    FGW_ROWS_CASE(160)
+    FGW_ROWS_CASE(176)
+    FGW_ROWS_CASE(192)
+    FGW_ROWS_CASE(208)
+    FGW_ROWS_CASE(224)
+    FGW_ROWS_CASE(240)
+    FGW_ROWS_CASE(256)
+#undef FGW_ROWS_CASE
+    default:
+      return 1;
+  }
+}
+
+static int gcd_int(int x, int y) {
+  while (y) {
+    const int t = x % y;
+    x = y;
+    y = t;
+  }
+  return x;
+}
+
+static bool make_kv_map(CUtensorMap* map, const void* base, const fgw_mha_params& p, int box_rows) {
+  const cuuint64_t dims[3] = {(cuuint64_t)p.head_dim, (cuuint64_t)p.heads, (cuuint64_t)p.pool_rows};
+  const cuuint64_t strides[2] = {(cuuint64_t)p.head_dim * 2, (cuuint64_t)p.heads * p.head_dim * 2};
+  const cuuint32_t box[3] = {(cuuint32_t)p.head_dim, 1, (cuuint32_t)box_rows};
+  const cuuint32_t estride[3] = {1, 1, 1};
+  const CUtensorMapDataType dt =
+      p.dtype == FGW_DTYPE_BFLOAT16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = encode_tiled()(map, dt, 3, const_cast<void*>(base), dims, strides, box, estride,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+cudaError_t launch_decode(const LaunchDesc& d, bool write_partials) {
+  const fgw_mha_params& p = d.p;
+  const int rows = decode_rows_per_item(p.head_dim);
+  DecodeArgs args;
+  args.q = p.q;
+  args.out = p.out;
+  args.table = p.block_table;
+  args.lengths = d.lens;
+  args.order = d.order;
+  args.part_o = d.part_o;
+  args.part_lse = d.part_lse;
+  args.ws = d.header;
+  args.batch = p.batch;
+  args.sq = p.q_len;
+  args.heads = p.heads;
+  args.width = p.table_width;
+  args.page = p.page_size;
+  args.splits = p.num_splits;
+  args.causal = p.causal;
+  args.row_blocks = (p.q_len + rows - 1) / rows;
+  args.box_rows = gcd_int(p.page_size, 64);
+  args.write_partials = write_partials ? 1 : 0;
+  args.items = (long long)p.batch * args.row_blocks * p.num_splits * p.heads;
+  args.scale_log2 = (1.0f / sqrtf((float)p.head_dim)) * kLog2e;
+  args.budget_ns = d.budget_ns;
+
+  CUtensorMap kmap, vmap;
+  if (!make_kv_map(&kmap, p.k_cache, p, args.box_rows) || !make_kv_map(&vmap, p.v_cache, p, args.box_rows)) {
+    return cudaErrorInvalidValue;
+  }
+  const bool bf16 = p.dtype == FGW_DTYPE_BFLOAT16;
+  switch (p.head_dim) {
+#define FGW_DECODE_CASE(DD)                                                          \
+  case DD:                                                                           \
+    return bf16 ? launch_decode_t<__nv_bfloat16, DD>(d, args, kmap, vmap)            \
+                : launch_decode_t<__half, DD>(d, args, kmap, vmap);
+    FGW_DECODE_CASE(16)
+    FGW_DECODE_CASE(32)
+    FGW_DECODE_CASE(48)
+    FGW_DECODE_CASE(64)
+    FGW_DECODE_CASE(80)
+    FGW_DECODE_CASE(96)
+    FGW_DECODE_CASE(112)
+    FGW_DECODE_CASE(128)
+    FGW_DECODE_CASE(144)
+    FGW_DECODE_CASE(160)
+    FGW_DECODE_CASE(176)
+    FGW_DECODE_CASE(192)
+    FGW_DECODE_CASE(208)
+    FGW_DECODE_CASE(224)
+    FGW_DECODE_CASE(240)
+    FGW_DECODE_CASE(256)
+#undef FGW_DECODE_CASE
+    default:
+      return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace fgw

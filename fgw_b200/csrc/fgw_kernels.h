@@ -1,0 +1,47 @@
+// Internal launch interface between the C ABI (fgw_api.cu) and the kernel translation units.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "fgw_mha.h"
+
+namespace fgw {
+
+struct WorkspaceHeader;
+
+// Resolved launch description shared by every kernel family.
+struct LaunchDesc {
+  fgw_mha_params p;
+  // workspace carve-up (device pointers)
+  WorkspaceHeader* header;
+  int32_t* lens;      // [batch] cache lengths clamped into [0, table_width * page_size]
+  int32_t* order;     // [batch] batch rows by descending cache length
+  float* part_o;      // [batch*q_len*heads, splits, head_dim] FP32 normalised partial outputs
+  float* part_lse;    // [batch*q_len*heads, splits] base-2 LSE per partial
+  uint64_t budget_ns;
+  int sm_count;
+  cudaStream_t stream;
+};
+
+// Workspace layout: header | lens | order | part_lse | part_o, each 256-byte aligned.
+size_t workspace_bytes(const fgw_mha_params& p, int path);
+void carve_workspace(LaunchDesc& d, void* workspace, int path);
+
+// Kernel launchers (return a cudaError_t from the launch).
+cudaError_t launch_plan(const LaunchDesc& d);
+cudaError_t launch_decode(const LaunchDesc& d, bool write_partials);
+cudaError_t launch_merge(const LaunchDesc& d);
+cudaError_t launch_tensor(const LaunchDesc& d, bool write_partials);
+
+// Which path AUTO picks.
+int resolve_path(const fgw_mha_params& p);
+
+// Tensor-map encoder from the driver (resolved once through the runtime).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn encode_tiled();
+
+}  // namespace fgw

@@ -1,0 +1,114 @@
+"""Latency model used to pick the split count of the general route, generalised over core count.
+
+Restates ``operators/mha/general_split_cost_model.py:44-91`` of FGW:
+
+* features over 32-token tiles with the head dimension padded to max(32, pow2(D)) / 64, waves over
+  the core count, mean live tiles per request, merge work and partial traffic (:109-132); version 2
+  adds the longest partition's excess over the mean (:128-131);
+* ``predict_us`` = max(linear model, latency floor of single- or multi-split launches) (:135-139);
+* ``select_model_splits`` keeps every split within tolerance of the best prediction and returns the
+  smallest (version 1: 2 % relative; version 2: max(2 %, absolute margin)) (:142-156).
+
+``cores=28`` with the reference coefficients (``models/reference_general_split_cost_model_v*.json``)
+reproduces the reference bit for bit; the reference's constants 28 and 56 are ``cores`` and
+``2 * cores``. B200 uses ``cores`` = the SM count and ``models/b200_general_split_cost_model.json``.
+"""
+import functools
+import json
+import math
+import pathlib
+
+from fgw_b200.operators.mha.general_split_policy import SPLITS
+
+MODEL_DIR = pathlib.Path(__file__).with_name("models")
+FEATURE_NAMES = (
+    "constant", "wave_tiles_times_padded_d", "wave_tiles", "waves_times_padded_d",
+    "waves", "has_merge", "merge_rows_times_splits_times_padded_d",
+    "partial_tasks_times_splits_times_padded_d",
+)
+FEATURE_NAMES_V2 = FEATURE_NAMES + ("longest_partition_excess_times_padded_d", "longest_partition_excess")
+
+
+def model_path(version=1):
+    if type(version) is not int or version not in (1, 2):
+        raise ValueError("General model version must be1 or2")
+    return MODEL_DIR / f"reference_general_split_cost_model_v{version}.json"
+
+
+def feature_names(version=1):
+    model_path(version)
+    return FEATURE_NAMES if version == 1 else FEATURE_NAMES_V2
+
+
+@functools.lru_cache(maxsize=8)
+def load_model(version=1, path=None):
+    model = json.loads(pathlib.Path(path or model_path(version)).read_text(encoding="utf-8"))
+    names = feature_names(model["version"])
+    if model["version"] != version or list(model["feature_names"]) != list(names) \
+            or len(model["weights"]) != len(names):
+        raise ValueError("General split model feature mismatch")
+    if any(not math.isfinite(v) or v < 0 for v in model["weights"]):
+        raise ValueError("General split model requires finite nonnegative weights")
+    return model
+
+
+def features(batch, sq, heads, dim, lengths, splits, version=1, cores=28):
+    feature_names(version)
+    if min(batch, sq, heads) <= 0 or not 16 <= dim <= 256 or dim % 16:
+        raise ValueError("Positive B/Q/H and D16..256 step16 required")
+    if len(lengths) != batch or any(type(n) is not int or n < 0 for n in lengths):
+        raise ValueError("One nonnegative integer cache length per request required")
+    if type(splits) is not int or splits not in SPLITS:
+        raise ValueError("Unsupported split count")
+    padded_d = max(32, 1 << (dim - 1).bit_length()) / 64
+    tasks = batch * heads * ((sq + 31) // 32)
+    waves = (tasks * splits + cores - 1) // cores
+    mean_tiles = sum((n + 31) // 32 for n in lengths) / batch
+    merge_rows = min(8, 1 << (sq - 1).bit_length())
+    merge_work = batch * heads * ((sq + merge_rows - 1) // merge_rows)
+    multi = 1 if splits > 1 else 0
+    values = [1.0,
+              waves * mean_tiles / splits * padded_d,
+              waves * mean_tiles / splits,
+              waves * padded_d,
+              float(waves),
+              float(multi),
+              multi * merge_work * splits * padded_d / (2 * cores),
+              multi * tasks * splits * padded_d / cores]
+    if version == 2:
+        longest = (max((n + 31) // 32 for n in lengths) + splits - 1) // splits
+        excess = max(0.0, longest - mean_tiles / splits)
+        values += [excess * padded_d, excess]
+    return values
+
+
+def predict_us(batch, sq, heads, dim, lengths, splits, model=None, version=1, cores=None):
+    model = load_model(version) if model is None else model
+    cores = model.get("cores", 28) if cores is None else cores
+    # The builtin sum (compensated on CPython >= 3.12), exactly as the reference accumulates.
+    raw = sum(a * b for a, b in zip(features(batch, sq, heads, dim, lengths, splits, model["version"], cores),
+                                    model["weights"]))
+    floor = model["latency_floor_us"]["multi" if splits > 1 else "single"]
+    return max(raw, floor)
+
+
+def select_model_splits(batch, sq, heads, dim, page_size, width, lengths, model=None, version=1, cores=None):
+    if page_size <= 0 or page_size % 16 or width <= 0:
+        raise ValueError("Positive page16-multiple and table width required")
+    if lengths is None:
+        raise ValueError("Experimental cost model requires host-known cache_lengths")
+    if len(lengths) != batch or any(n > page_size * width for n in lengths):
+        raise ValueError("cache_lengths must match batch and page-table capacity")
+    model = load_model(version) if model is None else model
+    capacity_tiles = (page_size * width + 31) // 32
+    costs = {}
+    for s in SPLITS:
+        if s <= capacity_tiles:
+            costs[s] = predict_us(batch, sq, heads, dim, lengths, s, model, cores=cores)
+    best = min(costs.values())
+    tolerance = model["selection_tolerance"]
+    if model["version"] == 1:
+        limit = best * (1 + tolerance)
+    else:
+        limit = best + max(best * tolerance, model.get("absolute_selection_margin_us", 0.0))
+    return min(s for s, value in costs.items() if value <= limit)

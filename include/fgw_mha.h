@@ -1,0 +1,130 @@
+/*
+ * fgw_mha.h -- C ABI of the B200 (sm_100a) paged multi-head-attention forward.
+ *
+ * One shared library, libfgw_mha.so, exports these entry points. Arguments are plain device
+ * pointers, sizes and a CUDA stream handle passed as void*; no framework types cross the
+ * boundary. Every call is asynchronous on the given stream and returns an fgw_status for
+ * argument and launch errors; device-side errors (a bounded wait that gave up) are recorded in
+ * the workspace header and read back with fgw_mha_read_error.
+ *
+ * Reference interfaces replaced (paths inside zhangwenhao91/FGW):
+ *   fgw_mha_paged_fwd       the launch callable returned by build_kernel and invoked by
+ *                           mha_paged_decode: operators/mha/kernels/mha_paged_decode_ascend_v7.py:471-473
+ *                           (direct, one split), :495-498 (partial then merge), :570 (call site);
+ *                           general route: mha_paged_decode_ascend_cube_general.py:186-187, 284-288.
+ *   fgw_mha_partial         the split-KV `partial` prim_func: v7.py:225-315 (compiled at :488-490),
+ *                           cube_general.py:192-222.
+ *   fgw_mha_merge           the LSE-weighted `merge` prim_func: v7.py:317-371, cube_general.py:224-279.
+ *   fgw_mha_workspace_size  the per-call Parts/LSE buffers the reference allocates as kernel outputs
+ *                           (v7.py:116, 232-233; out_idx=[5, 6] at :489).
+ *   fgw_mha_device_sm_count the core count the reference reads from the device properties
+ *                           (v7.py:65-68, 104-107 `cube_core_num`).
+ */
+#ifndef FGW_MHA_H_
+#define FGW_MHA_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FGW_MHA_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define FGW_API __attribute__((visibility("default")))
+#else
+#define FGW_API
+#endif
+
+typedef enum fgw_status {
+  FGW_OK = 0,
+  FGW_ERR_INVALID_ARGUMENT = 1,    /* shape, dtype, pointer or alignment precondition failed */
+  FGW_ERR_UNSUPPORTED = 2,         /* valid request this build does not implement */
+  FGW_ERR_WORKSPACE_TOO_SMALL = 3, /* workspace_bytes < fgw_mha_workspace_size(...) */
+  FGW_ERR_CUDA = 4,                /* a CUDA runtime/driver call or a launch failed */
+  FGW_ERR_DEVICE_TIMEOUT = 5,      /* a device-side bounded wait gave up (read via fgw_mha_read_error) */
+  FGW_ERR_NO_DEVICE = 6            /* no sm_100 device is current */
+} fgw_status;
+
+typedef enum fgw_dtype { FGW_DTYPE_FLOAT16 = 0, FGW_DTYPE_BFLOAT16 = 1 } fgw_dtype;
+
+/* Which kernel family runs the QK^T -> softmax -> PV body. */
+typedef enum fgw_path {
+  FGW_PATH_AUTO = 0,   /* decode kernel for short query blocks, tensor-core kernel otherwise */
+  FGW_PATH_DECODE = 1, /* warp-level HBM-streaming kernel (any q_len; intended for q_len <= 8) */
+  FGW_PATH_TENSOR = 2  /* tcgen05/TMEM kernel, 128-row query tiles */
+} fgw_path;
+
+/*
+ * Tensor contract (same as the reference, operators/mha/README.md:5):
+ *   q        [batch, q_len, heads, head_dim]      fp16/bf16, contiguous
+ *   k_cache  [pool_rows, heads, head_dim]         same dtype, contiguous, read-only
+ *   v_cache  [pool_rows, heads, head_dim]         same dtype, contiguous, read-only
+ *   block_table   [batch, table_width] int32      physical page ids (trusted, not range-checked)
+ *   cache_seqlens [batch] int32                   0 <= len <= table_width * page_size
+ *   out      [batch, q_len, heads, head_dim]      same dtype as q, written
+ * Logical token t of request b lives at pool row block_table[b, t / page_size] * page_size
+ * + t % page_size. Causal masking is right-aligned: query row i sees the first
+ * max(len - q_len + i + 1, 0) tokens. Rows that see no token are written as exact zeros.
+ */
+typedef struct fgw_mha_params {
+  const void* q;
+  const void* k_cache;
+  const void* v_cache;
+  const int32_t* block_table;
+  const int32_t* cache_seqlens;
+  void* out;
+  int64_t pool_rows;
+  int32_t batch;
+  int32_t q_len;
+  int32_t heads;
+  int32_t head_dim;    /* 16..256, multiple of 16 */
+  int32_t table_width;
+  int32_t page_size;   /* positive multiple of 16 dividing pool_rows */
+  int32_t dtype;       /* fgw_dtype */
+  int32_t causal;      /* 0 or 1 */
+  int32_t num_splits;  /* split-KV partitions per query block, >= 1 (1 = direct output) */
+  int32_t grid_cap;    /* persistent CTAs for the main kernel; 0 = one per work item */
+  int32_t path;        /* fgw_path */
+  int32_t wait_budget_ms; /* device-side wait limit; 0 = default (2000 ms) */
+  int32_t reserved[4];    /* must be zero */
+} fgw_mha_params;
+
+/* ABI version of the loaded library (FGW_MHA_ABI_VERSION it was built with). */
+FGW_API int fgw_mha_abi_version(void);
+
+/* Human-readable name of a status code (static storage). */
+FGW_API const char* fgw_mha_status_string(int status);
+
+/* Streaming multiprocessors of a CUDA device (148 on B200). */
+FGW_API int fgw_mha_device_sm_count(int device, int* sm_count);
+
+/* Kernel path AUTO resolves to for these parameters (FGW_PATH_DECODE or FGW_PATH_TENSOR). */
+FGW_API int fgw_mha_resolve_path(const fgw_mha_params* params, int* path);
+
+/* Bytes of device workspace fgw_mha_paged_fwd / fgw_mha_partial need for these parameters. */
+FGW_API int fgw_mha_workspace_size(const fgw_mha_params* params, size_t* bytes);
+
+/* Full forward: direct output when num_splits == 1, otherwise partial + merge, on `stream`.
+ * `workspace` must be 256-byte aligned device memory of at least fgw_mha_workspace_size bytes.
+ * The workspace header's error word is cleared at the start of every call. */
+FGW_API int fgw_mha_paged_fwd(const fgw_mha_params* params, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Split-KV partial only: writes FP32 per-split normalised outputs and base-2 LSEs into the
+ * workspace, for fgw_mha_merge to combine. Requires num_splits >= 2. */
+FGW_API int fgw_mha_partial(const fgw_mha_params* params, void* workspace, size_t workspace_bytes, void* stream);
+
+/* LSE-weighted merge of the partials fgw_mha_partial left in `workspace` into params->out. */
+FGW_API int fgw_mha_merge(const fgw_mha_params* params, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Synchronises `stream`, then reports the device-side status recorded in the workspace header
+ * (FGW_OK or FGW_ERR_DEVICE_TIMEOUT) and which wait site gave up (0 when clean). */
+FGW_API int fgw_mha_read_error(const void* workspace, void* stream, int* device_status, int* site);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FGW_MHA_H_ */
