@@ -1,0 +1,547 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 paged-MHA forward (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl fgw_b200|reference]
+    torchrun --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N ...
+
+Headline workload (the one the reference's headline MFU is quoted on):
+B2 H8 Q4096 KV2048 BF16 D128, 128-token pages with a shuffled block table, non-causal, N(0,1)
+synthetic data. A step is one forward call over that batch. With N GPUs every rank runs its own
+batch of 2 (weak scaling: per-GPU work fixed, global batch 2N), with no collective on the data path.
+The L2 (126 MB) is flushed with a 256 MiB write before every timed step, since the step's inputs
+(50 MB) would otherwise stay cached.
+
+Also measured in the same line (``decode``): BASELINE config 5, B256 H32 Q1 KV log-uniform in
+[1024, 32768], BF16 D128, 64-token pages scattered in a shared pool (~38 GB of K+V), sharded by head
+across the N ranks (strong scaling: whole-box microseconds per call, max over ranks).
+
+``--impl reference`` times the reference algorithm on the host cores instead: FGW's CPU FP32
+reference restated in NumPy (``oracle/``; the reference itself is Python on an Ascend stack and cannot
+run here), on the same headline workload, rank 0 only.
+"""
+import argparse
+import json
+import math
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+import torch
+
+ROOT = pathlib.Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "µs/call + % roofline (TC TFLOP/s long-Q, HBM GB/s decode) at 1/2/4/8 B200"
+LONGQ = dict(batch=2, sq=4096, heads=8, dim=128, page=128, kv=2048)
+DECODE = dict(batch=256, sq=1, heads=32, dim=128, page=64, kv_lo=1024, kv_hi=32768)
+ASCEND_V7_TFLOPS = 237.4  # v7 persistent28, B2H8 Q4096 KV2048, Ascend 950PR
+FLUSH_BYTES = 256 << 20
+
+
+def parse_args(argv=None):
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["fgw_b200", "reference"], default="fgw_b200")
+    p.add_argument("--no-decode", action="store_true", help="skip the config-5 decode measurement")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--path", choices=["auto", "decode", "tensor"], default="auto")
+    p.add_argument("--splits", type=int, default=None, help="force num_splits for the headline workload")
+    p.add_argument("--only", choices=["longq", "decode"], default=None, help="measure one workload (profiling)")
+    p.add_argument("--decode-batch", type=int, default=DECODE["batch"],
+                   help="requests in the decode workload (smaller values make profiling captures small)")
+    return p.parse_args(argv)
+
+
+# ----------------------------------------------------------------------------------------------- setup
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def init_dist(world, local):
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(value, world):
+    if world == 1:
+        return value
+    import torch.distributed as dist
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(value, world):
+    if world == 1:
+        return value
+    import torch.distributed as dist
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+def measured_peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return data["hbm_gbs"], data["bf16_tflops"], "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+# ---------------------------------------------------------------------------------------------- inputs
+def longq_inputs(seed, device):
+    c = LONGQ
+    width = c["kv"] // c["page"]
+    gen = torch.Generator().manual_seed(seed)
+    table = torch.randperm(c["batch"] * width, generator=gen).reshape(c["batch"], width).to(torch.int32)
+    lengths = torch.full((c["batch"],), c["kv"], dtype=torch.int32)
+    pool_rows = c["batch"] * width * c["page"]
+    gdev = torch.Generator(device=device).manual_seed(seed)
+    q = torch.randn(c["batch"], c["sq"], c["heads"], c["dim"], generator=gdev, device=device).to(torch.bfloat16)
+    k = torch.randn(pool_rows, c["heads"], c["dim"], generator=gdev, device=device).to(torch.bfloat16)
+    v = torch.randn(pool_rows, c["heads"], c["dim"], generator=gdev, device=device).to(torch.bfloat16)
+    return {"q": q, "k": k, "v": v, "table": table.to(device), "lengths": lengths.to(device),
+            "host_lengths": lengths.tolist(), "width": width, "page": c["page"], "causal": False}
+
+
+def decode_lengths(seed, batch):
+    c = DECODE
+    rng = np.random.default_rng(seed)
+    logs = rng.uniform(math.log(c["kv_lo"]), math.log(c["kv_hi"]), size=batch)
+    return np.minimum(np.floor(np.exp(logs)).astype(np.int64), c["kv_hi"])
+
+
+def decode_inputs(seed, rank, world, device, batch):
+    """Config 5, head-sharded: this rank holds heads [rank*H/N, (rank+1)*H/N) of every page."""
+    c = dict(DECODE, batch=batch)
+    lengths = decode_lengths(seed, batch)
+    pages_per = (lengths + c["page"] - 1) // c["page"]
+    width = int(pages_per.max())
+    total_pages = int(pages_per.sum())
+    rng = np.random.default_rng(seed + 1)
+    perm = rng.permutation(total_pages + 8)[:total_pages]  # pages scattered over a slightly larger pool
+    table = np.zeros((c["batch"], width), dtype=np.int32)
+    start = 0
+    for b, n in enumerate(pages_per):
+        table[b, :n] = perm[start:start + n]
+        start += n
+    pool_rows = (total_pages + 8) * c["page"]
+    heads = c["heads"] // world
+    gdev = torch.Generator(device=device).manual_seed(seed + 17 * rank)
+    q = torch.randn(c["batch"], 1, heads, c["dim"], generator=gdev, device=device).to(torch.bfloat16)
+    k = torch.empty(pool_rows, heads, c["dim"], dtype=torch.bfloat16, device=device)
+    v = torch.empty_like(k)
+    chunk = 1 << 20
+    for t in (k, v):
+        flat = t.view(-1)
+        for i in range(0, flat.numel(), chunk * 64):
+            n = min(chunk * 64, flat.numel() - i)
+            flat[i:i + n] = torch.randn(n, generator=gdev, device=device, dtype=torch.float32).to(torch.bfloat16)
+    return {"q": q, "k": k, "v": v, "table": torch.from_numpy(table).to(device),
+            "lengths": torch.from_numpy(lengths.astype(np.int32)).to(device), "host_lengths": lengths.tolist(),
+            "width": width, "page": c["page"], "causal": False, "heads": heads}
+
+
+# --------------------------------------------------------------------------------------------- helpers
+class ClockSampler:
+    """nvidia-smi clock/throttle sampling while the timed region runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index):
+        self.device_index = device_index
+        self.proc = None
+        self.file = None
+
+    def __enter__(self):
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.device_index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader",
+                 "-lms", "200"], stdout=self.file, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        self.file.flush()
+
+    def summary(self):
+        rows = []
+        try:
+            text = pathlib.Path(self.file.name).read_text()
+        finally:
+            os.unlink(self.file.name)
+        for line in text.splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1].split()[0]), float(parts[2].split()[0]), parts[5:9]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"], "samples": 0}
+        loaded = [r for r in rows if r[0] > 500] or rows
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in loaded for i, flag in enumerate(r[2]) if flag.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in loaded), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": reasons, "samples": len(rows)}
+
+
+def timed_steps(step_fns, steps, warmup, flush, stream):
+    """Run warmup + steps; per step, flush L2 (untimed) then time each stage with events.
+
+    step_fns: list of (name, fn) run in order each step. Returns {name: [ms per step]} and total list.
+    """
+    for _ in range(warmup):
+        for _, fn in step_fns:
+            fn()
+    torch.cuda.synchronize()
+    per = {name: [] for name, _ in step_fns}
+    totals = []
+    events = [[torch.cuda.Event(enable_timing=True) for _ in range(len(step_fns) + 1)] for _ in range(steps)]
+    for i in range(steps):
+        if flush is not None:
+            flush.zero_()
+        ev = events[i]
+        ev[0].record(stream)
+        for j, (_, fn) in enumerate(step_fns):
+            fn()
+            ev[j + 1].record(stream)
+    torch.cuda.synchronize()
+    for i in range(steps):
+        ev = events[i]
+        for j, (name, _) in enumerate(step_fns):
+            per[name].append(ev[j].elapsed_time(ev[j + 1]))
+        totals.append(ev[0].elapsed_time(ev[-1]))
+    return per, totals
+
+
+def flops_of(inp, sq, heads, dim):
+    from oracle import useful_flops  # the reference's FLOP policy (bench_mha_mfu.py:63-66)
+    return useful_flops(inp["host_lengths"], sq, heads, dim, inp["causal"])
+
+
+def bytes_of(inp, batch, sq, heads, dim):
+    from oracle import algorithmic_bytes
+    return algorithmic_bytes(inp["host_lengths"], batch, sq, heads, dim, inp["width"], 2)
+
+
+# ------------------------------------------------------------------------------------------ our kernels
+def run_longq(args, rank, world, device, stream):
+    from fgw_b200.operators.mha.current import build_kernel, mha_paged_decode
+    c = LONGQ
+    inp = longq_inputs(1000 + rank, device)
+    kernel = build_kernel(c["batch"], c["sq"], c["heads"], c["dim"], inp["k"].shape[0], inp["width"], c["page"],
+                          False, "bfloat16", device.index, num_splits=args.splits,
+                          full_kv_cache=True, path=args.path)
+    ws = kernel.new_workspace(device)
+    out = torch.empty_like(inp["q"])
+    a = (inp["q"], inp["k"], inp["v"], inp["table"], inp["lengths"])
+    fns = [("plan", lambda: kernel.plan_kernel(*a, ws)), ("attend", lambda: kernel.attend_kernel(*a, ws, out))]
+    if kernel.num_splits > 1:
+        fns.append(("merge", lambda: kernel.merge_only(*a, ws, out)))
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=device)
+    flops = flops_of(inp, c["sq"], c["heads"], c["dim"])
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(device.index) as clocks:
+        per, totals = timed_steps(fns, args.steps, args.warmup, flush, stream)
+        torch.cuda.synchronize()
+        barrier(world)
+    step_ms = sum(totals) / len(totals)
+    attend_ms = sum(per["attend"]) / len(per["attend"])
+
+    # End to end through the public API: pinned host inputs -> device -> forward -> host output.
+    host = {k: inp[k].cpu().pin_memory() for k in ("q", "k", "v", "table", "lengths")}
+    dev_bufs = {k: torch.empty_like(inp[k]) for k in host}
+    host_out = torch.empty(inp["q"].shape, dtype=inp["q"].dtype, pin_memory=True)
+
+    def e2e_step():
+        for key in host:
+            dev_bufs[key].copy_(host[key], non_blocking=True)
+        o = mha_paged_decode(dev_bufs["q"], dev_bufs["k"], dev_bufs["v"], dev_bufs["table"], dev_bufs["lengths"],
+                             c["page"], False, num_splits=args.splits, path=args.path,
+                             cache_lengths=inp["host_lengths"])
+        host_out.copy_(o, non_blocking=True)
+
+    _, e2e_totals = timed_steps([("e2e", e2e_step)], max(3, args.steps // 2), 2, flush, stream)
+    e2e_ms = statistics.median(e2e_totals)
+    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    d2h = host_out.numel() * host_out.element_size()
+    # parity spot check of the benchmarked output (first request, first 256 query rows) against the oracle
+    ok = check_longq(inp, out)
+    return {"kernel": kernel, "inp": inp, "flops": flops, "step_ms": step_ms, "attend_ms": attend_ms,
+            "per": per, "e2e_ms": e2e_ms, "h2d": h2d, "d2h": d2h, "clocks": clocks.summary(), "parity": ok,
+            "launches_per_step": len(fns)}
+
+
+def check_longq(inp, out):
+    from oracle import paged_attention
+    rows = 256
+    q = inp["q"][:1, :rows].float().cpu().numpy()
+    k = inp["k"].float().cpu().numpy()
+    v = inp["v"].float().cpu().numpy()
+    # causal=False: a prefix of the query rows attends to the same keys as in the full problem
+    want = paged_attention(q, k, v, inp["table"][:1].cpu().numpy(), np.array(inp["host_lengths"][:1]),
+                           inp["page"], False)
+    got = out[:1, :rows].float().cpu().numpy()
+    err = float(np.abs(got - want).max())
+    return {"rows_checked": rows, "max_abs_err": err, "pass": bool(err <= 2e-2)}
+
+
+def run_decode(args, rank, world, device, stream):
+    from fgw_b200.operators.mha.current import build_kernel
+    c = dict(DECODE, batch=args.decode_batch)
+    inp = decode_inputs(4242, rank, world, device, args.decode_batch)
+    heads = inp["heads"]
+    kernel = build_kernel(c["batch"], 1, heads, c["dim"], inp["k"].shape[0], inp["width"], c["page"], False,
+                          "bfloat16", device.index, cache_lengths=tuple(inp["host_lengths"]), path="decode")
+    ws = kernel.new_workspace(device)
+    out = torch.empty_like(inp["q"])
+    a = (inp["q"], inp["k"], inp["v"], inp["table"], inp["lengths"])
+    fns = [("plan", lambda: kernel.plan_kernel(*a, ws)), ("attend", lambda: kernel.attend_kernel(*a, ws, out))]
+    if kernel.num_splits > 1:
+        fns.append(("merge", lambda: kernel.merge_only(*a, ws, out)))
+    barrier(world)
+    torch.cuda.synchronize()
+    steps = max(5, args.steps // 2)
+    per, totals = timed_steps(fns, steps, max(3, args.warmup // 2), None, stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    step_ms = sum(totals) / len(totals)
+    attend_ms = sum(per["attend"]) / len(per["attend"])
+    nbytes = bytes_of(inp, c["batch"], 1, heads, c["dim"])
+    # parity spot check: 4 requests of this shard against the oracle
+    from oracle import paged_attention
+    idx = [0, 1, 2, 3]
+    ref_heads = min(heads, 2)
+    want = []
+    for b in idx:
+        n = inp["host_lengths"][b]
+        pages = inp["table"][b, : (n + c["page"] - 1) // c["page"]].long()
+        rows = (pages[:, None] * c["page"] + torch.arange(c["page"], device=device)[None, :]).reshape(-1)[:n]
+        kk = inp["k"][rows, :ref_heads]
+        vv = inp["v"][rows, :ref_heads]
+        q = inp["q"][b:b + 1, :, :ref_heads].float().cpu().numpy()
+        tbl = np.arange((n + c["page"] - 1) // c["page"], dtype=np.int32)[None]
+        want.append(paged_attention(q, _pad_pages(kk, c["page"]), _pad_pages(vv, c["page"]), tbl, np.array([n]),
+                                    c["page"], False)[0])
+    got = out[idx, :, :ref_heads].float().cpu().numpy()
+    err = float(max(np.abs(g - w).max() for g, w in zip(got, want)))
+    return {"kernel": kernel, "step_ms": step_ms, "attend_ms": attend_ms, "bytes": nbytes, "per": per,
+            "parity": {"requests_checked": len(idx), "max_abs_err": err, "pass": bool(err <= 2e-2)},
+            "launches_per_step": len(fns), "steps": steps}
+
+
+def _pad_pages(t, page):
+    rows = t.shape[0]
+    padded = (rows + page - 1) // page * page
+    out = torch.zeros((padded,) + tuple(t.shape[1:]), dtype=torch.float32, device=t.device)
+    out[:rows] = t.float()
+    return out.cpu().numpy()
+
+
+# ----------------------------------------------------------------------------------------- CPU baseline
+def cpu_threads():
+    try:
+        from threadpoolctl import threadpool_info
+        info = threadpool_info()
+        counts = [i.get("num_threads", 1) for i in info if i.get("internal_api") in ("openblas", "mkl", "blis")]
+        if counts:
+            return max(counts)
+    except Exception:
+        pass
+    return os.cpu_count() or 1
+
+
+def cpu_longq_sample(budget_s=12.0):
+    """Times the NumPy oracle on the headline workload, growing the sample until ~budget_s of work."""
+    from oracle import paged_attention_chunked, useful_flops
+    c = LONGQ
+    width = c["kv"] // c["page"]
+    rng = np.random.default_rng(5)
+    table = rng.permutation(c["batch"] * width).reshape(c["batch"], width).astype(np.int32)
+    pool = c["batch"] * width * c["page"]
+    k = rng.standard_normal((pool, c["heads"], c["dim"]), dtype=np.float32)
+    v = rng.standard_normal((pool, c["heads"], c["dim"]), dtype=np.float32)
+    rows, heads = 256, 1
+    elapsed, flops, calls = 0.0, 0, 0
+    while True:
+        q = rng.standard_normal((1, rows, heads, c["dim"]), dtype=np.float32)
+        t0 = time.perf_counter()
+        paged_attention_chunked(q, k[:, :heads], v[:, :heads], table[:1], np.array([c["kv"]]), c["page"], False)
+        dt = time.perf_counter() - t0
+        elapsed += dt
+        flops += useful_flops([c["kv"]], rows, heads, c["dim"], False)
+        calls += 1
+        if elapsed >= budget_s or calls >= 64:
+            break
+        if dt < budget_s / 8:
+            if rows < c["sq"]:
+                rows *= 2
+            elif heads < c["heads"]:
+                heads *= 2
+    value = flops / elapsed / 1e12
+    return {"value": value, "unit": "TFLOP/s", "cores": cpu_threads(), "kind": "port",
+            "sample": f"{calls} oracle calls on slices of config 2 (last: 1 request, {rows} query rows, {heads} heads,"
+                      f" KV 2048), {elapsed:.1f} s of CPU work, NumPy FP32 restatement of FGW's reference()"}
+
+
+# ---------------------------------------------------------------------------------------- reference arm
+def reference_arm(args, rank, world):
+    if rank != 0:
+        return 0
+    from oracle import paged_attention_chunked, useful_flops
+    c = LONGQ
+    width = c["kv"] // c["page"]
+    rng = np.random.default_rng(5)
+    table = rng.permutation(c["batch"] * width).reshape(c["batch"], width).astype(np.int32)
+    pool = c["batch"] * width * c["page"]
+    k = rng.standard_normal((pool, c["heads"], c["dim"]), dtype=np.float32)
+    v = rng.standard_normal((pool, c["heads"], c["dim"]), dtype=np.float32)
+    q_full = rng.standard_normal((c["batch"], c["sq"], c["heads"], c["dim"]), dtype=np.float32)
+    lengths = np.full(c["batch"], c["kv"])
+    # size the per-step sample so the whole run stays within a few minutes
+    rows = c["sq"]
+    t0 = time.perf_counter()
+    paged_attention_chunked(q_full[:, :128], k, v, table, lengths, c["page"], False)
+    per_row = (time.perf_counter() - t0) / 128
+    budget = 150.0 / max(1, args.steps + args.warmup)
+    if per_row * rows > budget:
+        rows = max(128, int(budget / per_row) // 128 * 128)
+    q = q_full[:, :rows]
+    flops = useful_flops(lengths.tolist(), rows, c["heads"], c["dim"], False)
+    for _ in range(args.warmup):
+        paged_attention_chunked(q, k, v, table, lengths, c["page"], False)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        paged_attention_chunked(q, k, v, table, lengths, c["page"], False)
+        times.append(time.perf_counter() - t0)
+    ms = 1e3 * sum(times) / len(times)
+    value = flops / (ms * 1e-3) / 1e12
+    sample = (f"{rows} of 4096 query rows per request (B2 H8 KV2048 D128), FP32 NumPy restatement of FGW's CPU "
+              "reference, all host BLAS threads")
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "longq_b2h8_q4096_kv2048_bf16_d128_page128", "global_batch": LONGQ["batch"],
+                       "seq_len": LONGQ["sq"], "kv_len": LONGQ["kv"], "parallelism": "host"},
+            "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": cpu_threads(), "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------------------------------------- main
+def main(argv=None):
+    args = parse_args(argv)
+    rank, world, local = dist_env()
+    if args.impl == "reference":
+        return reference_arm(args, rank, world)
+    init_dist(world, local)
+    device = torch.device("cuda", local)
+    stream = torch.cuda.current_stream(device)
+    hbm_peak, tc_peak, peak_kind = measured_peaks()
+    line = {"metric": METRIC, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "scaling": "weak", "dtype": "bf16", "data": "synthetic"}
+    lq = None
+    if args.only in (None, "longq"):
+        lq = run_longq(args, rank, world, device, stream)
+        c = LONGQ
+        step_ms = max_over_ranks(lq["step_ms"], world)
+        attend_ms = max_over_ranks(lq["attend_ms"], world)
+        e2e_ms = max_over_ranks(lq["e2e_ms"], world)
+        total_flops = sum_over_ranks(lq["flops"], world)
+        achieved = lq["flops"] / (lq["attend_ms"] * 1e-3) / 1e12
+        traffic = None
+        prof = ROOT / "profiles" / "traffic_per_launch.json"
+        if prof.exists():
+            traffic = json.loads(prof.read_text()).get("longq_attend")
+        k = lq["kernel"]
+        line.update({
+            "value": total_flops / (step_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": step_ms,
+            "us_per_call": step_ms * 1e3,
+            "vs_baseline": (total_flops / (step_ms * 1e-3) / 1e12 / world) / ASCEND_V7_TFLOPS,
+            "config": {"workload": "longq_b2h8_q4096_kv2048_bf16_d128_page128", "global_batch": c["batch"] * world,
+                       "seq_len": c["sq"], "kv_len": c["kv"], "parallelism": f"batch-shard x{world}",
+                       "l2": "flushed (256 MiB write) before every timed step", "num_splits": k.num_splits,
+                       "execution_path": k.execution_path, "compute_grid": k.compute_grid,
+                       "vs_baseline_source": "BASELINE.md: 237.4 TFLOP/s, FGW v7 persistent28 on Ascend 950PR "
+                                             "(per GPU)"},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": tc_peak, "unit": "TFLOP/s",
+                         "frac": achieved / tc_peak, "traffic": traffic,
+                         "kernel": "attend (" + k.execution_path + ")", "peak_source": f"{peak_kind} bf16_tflops"},
+            "e2e": {"value": total_flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": lq["h2d"], "d2h_bytes_per_step": lq["d2h"], "ms_per_step": e2e_ms},
+            "clocks": lq["clocks"], "parity": lq["parity"],
+            "gpu_launches": lq["launches_per_step"] * args.steps,
+            "stage_ms": {n: statistics.mean(v) for n, v in lq["per"].items()},
+        })
+    if not args.no_decode and args.only in (None, "decode"):
+        dc = run_decode(args, rank, world, device, stream)
+        step_ms = max_over_ranks(dc["step_ms"], world)
+        attend_ms = max_over_ranks(dc["attend_ms"], world)
+        total_bytes = sum_over_ranks(dc["bytes"], world)
+        args_batch = args.decode_batch
+        achieved = dc["bytes"] / (dc["attend_ms"] * 1e-3) / 1e9
+        k = dc["kernel"]
+        decode = {"workload": f"decode_b{args.decode_batch}h32_q1_kvlogu1024_32768_bf16_d128_page64",
+                  "scaling": "strong",
+                  "parallelism": f"head-shard x{world}", "us_per_call": step_ms * 1e3,
+                  "value": total_bytes / (step_ms * 1e-3) / 1e9, "unit": "GB/s",
+                  "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                               "frac": achieved / hbm_peak, "kernel": "attend (" + k.execution_path + ")",
+                               "peak_source": f"{peak_kind} hbm_gbs"},
+                  "num_splits": k.num_splits, "parity": dc["parity"],
+                  "gpu_launches": dc["launches_per_step"] * dc["steps"],
+                  "stage_ms": {n: statistics.mean(v) for n, v in dc["per"].items()}}
+        line["decode"] = decode
+        line["gpu_launches"] = line.get("gpu_launches", 0) + decode["gpu_launches"]
+        if lq is None:
+            line.update({"value": decode["value"], "unit": "GB/s", "ms_per_step": step_ms, "vs_baseline": None,
+                         "config": {"workload": decode["workload"]}, "roofline": decode["roofline"]})
+    if rank == 0 and world == 1 and args.only is None and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_longq_sample()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

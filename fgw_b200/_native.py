@@ -32,6 +32,8 @@ EXPORTED = (
     "fgw_mha_resolve_path",
     "fgw_mha_workspace_size",
     "fgw_mha_paged_fwd",
+    "fgw_mha_plan",
+    "fgw_mha_attend",
     "fgw_mha_partial",
     "fgw_mha_merge",
     "fgw_mha_read_error",
@@ -108,7 +110,7 @@ def library():
     lib.fgw_mha_resolve_path.restype = ctypes.c_int
     lib.fgw_mha_workspace_size.argtypes = [p, ctypes.POINTER(ctypes.c_size_t)]
     lib.fgw_mha_workspace_size.restype = ctypes.c_int
-    for name in ("fgw_mha_paged_fwd", "fgw_mha_partial", "fgw_mha_merge"):
+    for name in ("fgw_mha_paged_fwd", "fgw_mha_plan", "fgw_mha_attend", "fgw_mha_partial", "fgw_mha_merge"):
         fn = getattr(lib, name)
         fn.argtypes = [p, vp, ctypes.c_size_t, vp]
         fn.restype = ctypes.c_int
@@ -155,6 +157,15 @@ def workspace_size(params):
 def paged_fwd(params, workspace_ptr, workspace_bytes, stream_ptr):
     check(library().fgw_mha_paged_fwd(ctypes.byref(params), workspace_ptr, workspace_bytes, stream_ptr),
           "fgw_mha_paged_fwd")
+
+
+def plan(params, workspace_ptr, workspace_bytes, stream_ptr):
+    check(library().fgw_mha_plan(ctypes.byref(params), workspace_ptr, workspace_bytes, stream_ptr), "fgw_mha_plan")
+
+
+def attend(params, workspace_ptr, workspace_bytes, stream_ptr):
+    check(library().fgw_mha_attend(ctypes.byref(params), workspace_ptr, workspace_bytes, stream_ptr),
+          "fgw_mha_attend")
 
 
 def partial(params, workspace_ptr, workspace_bytes, stream_ptr):

@@ -194,6 +194,20 @@ int fgw_mha_paged_fwd(const fgw_mha_params* params, void* workspace, size_t work
   return FGW_OK;
 }
 
+int fgw_mha_plan(const fgw_mha_params* params, void* workspace, size_t workspace_bytes_given, void* stream) {
+  LaunchDesc d;
+  int st = prepare(params, workspace, workspace_bytes_given, stream, d);
+  if (st != FGW_OK) return st;
+  return launch_plan(d) == cudaSuccess ? FGW_OK : FGW_ERR_CUDA;
+}
+
+int fgw_mha_attend(const fgw_mha_params* params, void* workspace, size_t workspace_bytes_given, void* stream) {
+  LaunchDesc d;
+  int st = prepare(params, workspace, workspace_bytes_given, stream, d);
+  if (st != FGW_OK) return st;
+  return launch_main(d, d.p.num_splits > 1);
+}
+
 int fgw_mha_partial(const fgw_mha_params* params, void* workspace, size_t workspace_bytes_given, void* stream) {
   LaunchDesc d;
   int st = prepare(params, workspace, workspace_bytes_given, stream, d);

@@ -225,6 +225,16 @@ def build_kernel(batch, sq, heads, dim, pool_rows, width, page_size, causal, dty
         _native.paged_fwd(_bind(q, k, v, table, lengths, out), ws.data_ptr(), ws.numel(), stream)
         return out
 
+    def plan_kernel(q, k, v, table, lengths, workspace):
+        _native.plan(_bind(q, k, v, table, lengths, q), workspace.data_ptr(), workspace.numel(),
+                     torch.cuda.current_stream(q.device).cuda_stream)
+        return workspace
+
+    def attend_kernel(q, k, v, table, lengths, workspace, out):
+        _native.attend(_bind(q, k, v, table, lengths, out), workspace.data_ptr(), workspace.numel(),
+                       torch.cuda.current_stream(q.device).cuda_stream)
+        return out
+
     def partial_kernel(q, k, v, table, lengths, workspace):
         out = torch.empty_like(q)
         _native.partial(_bind(q, k, v, table, lengths, out), workspace.data_ptr(), workspace.numel(),
@@ -256,6 +266,9 @@ def build_kernel(batch, sq, heads, dim, pool_rows, width, page_size, causal, dty
     launch.general_model_version = general_model_version if policy_name == "cost_model" else None
     launch.prepare_q = lambda q: q  # Q is read in place through a 4-D TMA map; no head-major copy
     launch.new_workspace = _workspace
+    launch.plan_kernel = plan_kernel
+    launch.attend_kernel = attend_kernel
+    launch.merge_only = merge_kernel
     launch.params = params
     if splits == 1:
         launch.direct_kernel = launch

@@ -17,6 +17,9 @@
  *   fgw_mha_merge           the LSE-weighted `merge` prim_func: v7.py:317-371, cube_general.py:224-279.
  *   fgw_mha_workspace_size  the per-call Parts/LSE buffers the reference allocates as kernel outputs
  *                           (v7.py:116, 232-233; out_idx=[5, 6] at :489).
+ *   fgw_mha_plan / fgw_mha_attend  the two halves of fgw_mha_paged_fwd, exposed like the reference
+ *                           exposes its compiled kernels on the launch callable for isolated profiling
+ *                           (v7_experimental.py:842-855: direct_kernel / partial_kernel / merge_kernel).
  *   fgw_mha_device_sm_count the core count the reference reads from the device properties
  *                           (v7.py:65-68, 104-107 `cube_core_num`).
  */
@@ -111,6 +114,15 @@ FGW_API int fgw_mha_workspace_size(const fgw_mha_params* params, size_t* bytes);
  * `workspace` must be 256-byte aligned device memory of at least fgw_mha_workspace_size bytes.
  * The workspace header's error word is cleared at the start of every call. */
 FGW_API int fgw_mha_paged_fwd(const fgw_mha_params* params, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Planning pass alone: clears the workspace error word, clamps cache lengths into table capacity
+ * and orders requests by descending length for the persistent schedule. fgw_mha_paged_fwd runs it
+ * first; callers timing the attention kernel by itself run it once, then fgw_mha_attend. */
+FGW_API int fgw_mha_plan(const fgw_mha_params* params, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Attention kernel alone, over a workspace fgw_mha_plan has prepared: writes the output directly
+ * when num_splits == 1, else the split partials (follow with fgw_mha_merge). */
+FGW_API int fgw_mha_attend(const fgw_mha_params* params, void* workspace, size_t workspace_bytes, void* stream);
 
 /* Split-KV partial only: writes FP32 per-split normalised outputs and base-2 LSEs into the
  * workspace, for fgw_mha_merge to combine. Requires num_splits >= 2. */
