@@ -56,7 +56,7 @@ void carve_workspace(LaunchDesc& d, void* workspace, int /*path*/) {
 
 int resolve_path(const fgw_mha_params& p) {
   if (p.path == FGW_PATH_DECODE || p.path == FGW_PATH_TENSOR) return p.path;
-  return FGW_PATH_DECODE;
+  return p.q_len <= 8 ? FGW_PATH_DECODE : FGW_PATH_TENSOR;
 }
 
 static bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }

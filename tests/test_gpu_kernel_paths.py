@@ -1,0 +1,64 @@
+"""Each CUDA kernel family (forced through the C ABI path knob) against the reference golden outputs.
+
+``path="tensor"`` runs the tcgen05/TMEM kernel and ``path="decode"`` the warp-level kernel on every
+golden case, whatever the query length, so both kernels are held to the reference on every head
+dimension, page size, causal mode, length pattern and NaN-poisoned pool the fixtures cover.
+"""
+import pytest
+import torch
+
+from fixtures import build_case, dtype_name, oracle_output
+from golden_data import entry_params, expected_bits, output_index
+from oracle import dtype_bits_to_f32
+from test_gpu_parity import _check, _run
+
+pytestmark = pytest.mark.gpu
+
+ENTRIES = output_index()
+
+
+def test_tensor_path_smallest_case_first():
+    inputs = build_case(("tiny_tensor", 1, 130, 1, 128, 128, 2), 7, torch.bfloat16, False, "full")
+    out = _run(inputs, path="tensor")
+    _check(out, oracle_output(inputs), inputs)
+
+
+@pytest.mark.parametrize("path", ["tensor", "decode"])
+@pytest.mark.parametrize("entry", ENTRIES, ids=[e["key"] for e in ENTRIES])
+def test_kernel_path_matches_reference_golden(entry, path):
+    case, seed, dtype, causal, pattern = entry_params(entry)
+    inputs = build_case(case, seed, dtype, causal, pattern)
+    expected = dtype_bits_to_f32(expected_bits(entry), dtype_name(dtype))
+    _check(_run(inputs, path=path), expected, inputs)
+
+
+SPLIT_ENTRIES = [e for e in ENTRIES if e["seed"] == 7 and e["pattern"] == "mixed"]
+
+
+@pytest.mark.parametrize("splits", [2, 8])
+@pytest.mark.parametrize("entry", SPLIT_ENTRIES, ids=[e["key"] for e in SPLIT_ENTRIES])
+def test_tensor_path_splits_match_oracle(entry, splits):
+    case, seed, dtype, causal, pattern = entry_params(entry)
+    if splits > (case[5] * case[6] + 31) // 32:
+        pytest.skip("more splits than 32-token tiles in table capacity")
+    inputs = build_case(case, seed, dtype, causal, pattern)
+    _check(_run(inputs, path="tensor", cube_mode="general", num_splits=splits), oracle_output(inputs), inputs)
+
+
+@pytest.mark.parametrize("dim", [16, 48, 64, 80, 128, 144, 192, 256])
+@pytest.mark.parametrize("page", [16, 48, 64])
+def test_tensor_path_long_causal_tails(dim, page):
+    # Config-4 style: several 128-row query tiles, causal, ragged lengths incl. 0 and partial pages,
+    # 1% of K rows scaled x8 to stress the running max.
+    case = (f"edge_d{dim}_p{page}", 3, 200, 2, dim, page, (700 + page - 1) // page)
+    inputs = build_case(case, 2026, torch.float16, True, "mixed")
+    inputs["lengths"] = torch.tensor([0, 699, 333], dtype=torch.int32)
+    gen = torch.Generator().manual_seed(11)
+    rows = torch.randperm(inputs["k"].shape[0], generator=gen)[: max(1, inputs["k"].shape[0] // 100)]
+    k = inputs["k"].clone()
+    k[rows] = (k[rows].float() * 8).to(k.dtype)
+    inputs["k"] = k
+    from fixtures import poison_unread
+    inputs["k"], inputs["v"] = poison_unread(inputs["k"], inputs["v"], inputs["table"], inputs["lengths"].tolist(),
+                                             page)
+    _check(_run(inputs, path="tensor"), oracle_output(inputs), inputs)
