@@ -51,14 +51,14 @@ def test_tensor_path_long_causal_tails(dim, page):
     # Config-4 style: several 128-row query tiles, causal, ragged lengths incl. 0 and partial pages,
     # 1% of K rows scaled x8 to stress the running max.
     case = (f"edge_d{dim}_p{page}", 3, 200, 2, dim, page, (700 + page - 1) // page)
-    inputs = build_case(case, 2026, torch.float16, True, "mixed")
-    inputs["lengths"] = torch.tensor([0, 699, 333], dtype=torch.int32)
+    from fixtures import make_inputs, poison_unread
+    q, k, v, table = make_inputs(case, 2026, torch.float16)
+    lengths = [0, 699, 333]
     gen = torch.Generator().manual_seed(11)
-    rows = torch.randperm(inputs["k"].shape[0], generator=gen)[: max(1, inputs["k"].shape[0] // 100)]
-    k = inputs["k"].clone()
+    rows = torch.randperm(k.shape[0], generator=gen)[: max(1, k.shape[0] // 100)]
+    k = k.clone()
     k[rows] = (k[rows].float() * 8).to(k.dtype)
-    inputs["k"] = k
-    from fixtures import poison_unread
-    inputs["k"], inputs["v"] = poison_unread(inputs["k"], inputs["v"], inputs["table"], inputs["lengths"].tolist(),
-                                             page)
+    k, v = poison_unread(k, v, table, lengths, page)
+    inputs = {"case": case, "seed": 2026, "dtype": torch.float16, "causal": True, "pattern": "edge", "q": q,
+              "k": k, "v": v, "table": table, "lengths": torch.tensor(lengths, dtype=torch.int32)}
     _check(_run(inputs, path="tensor"), oracle_output(inputs), inputs)
