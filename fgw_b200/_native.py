@@ -37,7 +37,10 @@ EXPORTED = (
     "fgw_mha_partial",
     "fgw_mha_merge",
     "fgw_mha_read_error",
+    "fgw_mha_paged_fwd_static_ws",
 )
+
+STATIC_WORKSPACE_BYTES = 16 << 20  # FGW_MHA_STATIC_WORKSPACE_BYTES
 
 
 class NativeLibraryError(RuntimeError):
@@ -116,6 +119,8 @@ def library():
         fn.restype = ctypes.c_int
     lib.fgw_mha_read_error.argtypes = [vp, vp, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int)]
     lib.fgw_mha_read_error.restype = ctypes.c_int
+    lib.fgw_mha_paged_fwd_static_ws.argtypes = [p, vp]
+    lib.fgw_mha_paged_fwd_static_ws.restype = ctypes.c_int
     _LIB = lib
     return lib
 
@@ -185,3 +190,8 @@ def read_error(workspace_ptr, stream_ptr):
     check(library().fgw_mha_read_error(workspace_ptr, stream_ptr, ctypes.byref(status), ctypes.byref(site)),
           "fgw_mha_read_error")
     return status.value, site.value
+
+
+def paged_fwd_static_ws(params, stream_ptr):
+    """Forward with the library's own static scratch array: allocates nothing (see include/fgw_mha.h)."""
+    check(library().fgw_mha_paged_fwd_static_ws(ctypes.byref(params), stream_ptr), "fgw_mha_paged_fwd_static_ws")

@@ -1,0 +1,57 @@
+// Allocation-free variant of fgw_mha_paged_fwd.
+//
+// Some callers cannot call cudaMalloc at the point where they run attention: code running inside a
+// custom allocator or memory-pool callback, real-time serving loops that forbid allocator traffic
+// (and the device-wide synchronisation cudaFree implies), and plugins whose host framework owns all
+// device memory and hands out only input and output buffers. For them this entry point runs the same
+// plan / attention / merge kernels as fgw_mha_paged_fwd, but its scratch (workspace header, clamped
+// lengths, request order and split-KV partials) lives in one file-scope __device__ array of
+// FGW_MHA_STATIC_WORKSPACE_BYTES that every GPU loading the library holds until the process exits.
+//
+// The array's name is only a host-side stand-in in host code; its device address is looked up once
+// per device with cudaGetSymbolAddress (with that device current) on the first call made on that device,
+// and cached. Nothing here allocates.
+#include <mutex>
+
+#include "fgw_mha.h"
+
+#include <cuda_runtime.h>
+
+namespace {
+
+static __device__ __align__(256) unsigned char g_static_workspace[FGW_MHA_STATIC_WORKSPACE_BYTES];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_mutex;
+void* g_device_ptr[kMaxDevices] = {nullptr};
+
+// Device address of g_static_workspace on the current device (looked up on first use).
+int static_workspace_ptr(void** ptr) {
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= kMaxDevices) return FGW_ERR_NO_DEVICE;
+  std::lock_guard<std::mutex> lock(g_mutex);
+  if (g_device_ptr[device] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_static_workspace) != cudaSuccess || p == nullptr) return FGW_ERR_CUDA;
+    g_device_ptr[device] = p;
+  }
+  *ptr = g_device_ptr[device];
+  return FGW_OK;
+}
+
+}  // namespace
+
+extern "C" int fgw_mha_paged_fwd_static_ws(const fgw_mha_params* params, void* stream) {
+  if (params == nullptr) return FGW_ERR_INVALID_ARGUMENT;
+  size_t needed = 0;
+  int st = fgw_mha_workspace_size(params, &needed);
+  if (st != FGW_OK) return st;
+  if (needed > static_cast<size_t>(FGW_MHA_STATIC_WORKSPACE_BYTES)) return FGW_ERR_WORKSPACE_TOO_SMALL;
+  void* ws = nullptr;
+  st = static_workspace_ptr(&ws);
+  if (st != FGW_OK) return st;
+  // The plan kernel that starts every forward clears the error word; every other byte of scratch the
+  // kernels read (lengths, order, partials) is written earlier in the same call, so the previous
+  // call's leftovers never reach an output.
+  return fgw_mha_paged_fwd(params, ws, FGW_MHA_STATIC_WORKSPACE_BYTES, stream);
+}

@@ -131,6 +131,20 @@ FGW_API int fgw_mha_partial(const fgw_mha_params* params, void* workspace, size_
 /* LSE-weighted merge of the partials fgw_mha_partial left in `workspace` into params->out. */
 FGW_API int fgw_mha_merge(const fgw_mha_params* params, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Bytes of the library-owned scratch array fgw_mha_paged_fwd_static_ws uses (16 MiB per GPU). */
+#define FGW_MHA_STATIC_WORKSPACE_BYTES (16u << 20)
+
+/* Allocation-free forward, for callers that cannot allocate device memory where they run attention
+ * (inside an allocator or memory-pool callback, in a serving loop that forbids allocator calls, or in a
+ * plugin whose host owns all device memory). No counterpart in the reference, which allocates its
+ * scratch per call. Same kernels and results as fgw_mha_paged_fwd, but the workspace is a file-scope
+ * device array of FGW_MHA_STATIC_WORKSPACE_BYTES held by every GPU that loads the library until exit;
+ * nothing is allocated or freed. Returns FGW_ERR_WORKSPACE_TOO_SMALL when fgw_mha_workspace_size(params)
+ * exceeds that size. The first call on a device looks up the array's device address on the current
+ * device; make that first call before any stream capture. All calls share the one array, so calls that
+ * overlap on the GPU (different streams, or threads) race: serialise them. */
+FGW_API int fgw_mha_paged_fwd_static_ws(const fgw_mha_params* params, void* stream);
+
 /* Synchronises `stream`, then reports the device-side status recorded in the workspace header
  * (FGW_OK or FGW_ERR_DEVICE_TIMEOUT) and which wait site gave up (0 when clean). */
 FGW_API int fgw_mha_read_error(const void* workspace, void* stream, int* device_status, int* site);
