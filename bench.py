@@ -275,12 +275,31 @@ def run_longq(args, rank, world, device, stream):
     flops = flops_of(inp, c["sq"], c["heads"], c["dim"])
     barrier(world)
     torch.cuda.synchronize()
+    per, totals = timed_steps(fns, args.steps, args.warmup, flush, stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    eager_step_ms = sum(totals) / len(totals)
+    attend_ms = sum(per["attend"]) / len(per["attend"])
+
+    # The same step captured once as a CUDA graph and replayed: no host launch gaps between the planning
+    # and attention launches. This is the step time `value` reports.
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream(device)
+    side.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(side):
+        for _, fn in fns:
+            fn()
+    torch.cuda.current_stream(device).wait_stream(side)
+    with torch.cuda.graph(graph):
+        for _, fn in fns:
+            fn()
+    barrier(world)
+    torch.cuda.synchronize()
     with ClockSampler(device.index) as clocks:
-        per, totals = timed_steps(fns, args.steps, args.warmup, flush, stream)
+        _, graph_totals = timed_steps([("step", graph.replay)], args.steps, args.warmup, flush, stream)
         torch.cuda.synchronize()
         barrier(world)
-    step_ms = sum(totals) / len(totals)
-    attend_ms = sum(per["attend"]) / len(per["attend"])
+    step_ms = sum(graph_totals) / len(graph_totals)
 
     # End to end through the public API: pinned host inputs -> device -> forward -> host output.
     host = {k: inp[k].cpu().pin_memory() for k in ("q", "k", "v", "table", "lengths")}
@@ -301,7 +320,9 @@ def run_longq(args, rank, world, device, stream):
     d2h = host_out.numel() * host_out.element_size()
     # parity spot check of the benchmarked output (first request, first 256 query rows) against the oracle
     ok = check_longq(inp, out)
+    del graph
     return {"kernel": kernel, "inp": inp, "flops": flops, "step_ms": step_ms, "attend_ms": attend_ms,
+            "eager_step_ms": eager_step_ms,
             "per": per, "e2e_ms": e2e_ms, "h2d": h2d, "d2h": d2h, "clocks": clocks.summary(), "parity": ok,
             "launches_per_step": len(fns)}
 
@@ -509,6 +530,9 @@ def main(argv=None):
             "clocks": lq["clocks"], "parity": lq["parity"],
             "gpu_launches": lq["launches_per_step"] * args.steps,
             "stage_ms": {n: statistics.mean(v) for n, v in lq["per"].items()},
+            "eager_step_ms": max_over_ranks(lq["eager_step_ms"], world),
+            "step_timing": "CUDA-graph replay of plan+attend(+merge), L2 flushed before each step; stage_ms and "
+                           "roofline from per-launch events of the same step run eagerly",
         })
     if not args.no_decode and args.only in (None, "decode"):
         dc = run_decode(args, rank, world, device, stream)

@@ -3,6 +3,7 @@
 // cube_general.py:186-188, 284-288): one launch when there is one split, partial then merge
 // otherwise, all on the caller's stream. A small planning launch precedes them and replaces the
 // reference's host copy of the cache lengths (v7.py:548).
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -104,6 +105,16 @@ static int device_sm_count_cached(int device, int* sms) {
   return FGW_OK;
 }
 
+// FGW_MHA_TENSOR_SINGLE_TILE=1 selects the one-query-tile tensor kernel for every head dimension
+// (the two-tile kernel is the default for head_dim <= 128); read once per process.
+static bool single_tile_requested() {
+  static const bool value = [] {
+    const char* v = std::getenv("FGW_MHA_TENSOR_SINGLE_TILE");
+    return v != nullptr && v[0] == '1';
+  }();
+  return value;
+}
+
 static int prepare(const fgw_mha_params* params, void* workspace, size_t workspace_bytes_given, void* stream,
                    LaunchDesc& d) {
   int st = validate(params);
@@ -122,6 +133,7 @@ static int prepare(const fgw_mha_params* params, void* workspace, size_t workspa
   const int budget_ms = d.p.wait_budget_ms > 0 ? d.p.wait_budget_ms : 2000;
   d.budget_ns = static_cast<uint64_t>(budget_ms) * 1000000ull;
   d.stream = static_cast<cudaStream_t>(stream);
+  d.single_tile = single_tile_requested();
   return FGW_OK;
 }
 

@@ -1,0 +1,561 @@
+// Two-query-tile tensor-core paged attention for head dims up to 128 (the long-query workhorse).
+//
+// Same contract and masking rules as fmha_sm100_kernel (fgw_fmha_sm100.cu), which it replaces for D <= 128;
+// the reference body it stands for is operators/mha/kernels/mha_paged_decode_ascend_v7.py:225-315, 375-465.
+// What changes is the schedule:
+//   * a work item is a pair of 128-row query tiles (A, B) of one (request, head, split); both share every
+//     K/V tile, so K/V shared-memory traffic per FLOP halves;
+//   * two softmax warpgroups (warps 4-7 for A, 8-11 for B) ping-pong on the tensor core. The single MMA
+//     thread issues, per KV tile j:  PV_A(j), QK_A(j+1), PV_B(j), QK_B(j+1)  so the softmax of A(j+1)
+//     overlaps PV_B(j) + QK_B(j+1) and the softmax of B(j) overlaps PV_A(j) + QK_A(j+1);
+//   * P never touches shared memory: each softmax thread writes its bf16/fp16 P row back into the TMEM
+//     columns of the S row it has just consumed, and PV reads P straight from TMEM (tcgen05.mma with the
+//     A operand in tensor memory);
+//   * a commit after QK_t(j+1) also covers the earlier PV_t(j), so a softmax thread that has seen S_t(j+1)
+//     may rescale O_t in TMEM without a separate wait.
+// TMEM: S_A [0,128), S_B [128,256), O_A [256,256+D), O_B [384,384+D) of 512 columns.
+#include <algorithm>
+
+#include "fgw_common.cuh"
+#include "fgw_kernels.h"
+
+namespace fgw {
+
+struct Fmha2Args {
+  void* out;
+  const int32_t* table;
+  const int32_t* lengths;
+  const int32_t* order;
+  float* part_o;
+  float* part_lse;
+  WorkspaceHeader* ws;
+  int batch, sq, heads, dim, width, page, splits, causal, box_rows, write_partials, qpairs;
+  long long items;
+  float scale_log2;
+  uint64_t budget_ns;
+};
+
+template <int NB>
+struct Fmha2Shape {
+  static constexpr int kBN = 128;
+  static constexpr int kTileBytes = 128 * 128;           // one 64-col block of a 128-row operand
+  static constexpr int kQBytes = NB * kTileBytes;        // one 128-row query tile
+  static constexpr int kKVBytes = NB * kBN * 128;        // one K (or V) stage
+  static constexpr int kStages = NB == 1 ? 4 : 2;
+  static constexpr int kThreads = 384;
+  // TMEM column of S_t / O_t for query tile t
+  __device__ __forceinline__ static uint32_t s_col(int t) { return static_cast<uint32_t>(t) * 128u; }
+  __device__ __forceinline__ static uint32_t o_col(int t) { return 256u + static_cast<uint32_t>(t) * 128u; }
+  static constexpr int kTmemCols = 512;
+  // shared memory carve-up
+  static constexpr int kQ = 0;
+  static constexpr int kK = kQ + 2 * kQBytes;
+  static constexpr int kV = kK + kStages * kKVBytes;
+  static constexpr int kBar = kV + kStages * kKVBytes;
+  // q_full, q_empty, k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2], p_full[2], pv_done[2],
+  // o_empty[2], mma_done
+  static constexpr int kNumBars = 2 + 4 * kStages + 8 + 1;
+  static constexpr int kTmemSlot = kBar + kNumBars * 8;
+  static constexpr int kBytes = kTmemSlot + 16 + 1024;
+};
+
+struct PairItem {
+  int b, h, s, q0, len, n_begin, n, n_tile[2];
+};
+
+__device__ __forceinline__ int visible_upto(int row, int len, int sq, int causal) {
+  return causal ? max(len - sq + row + 1, 0) : len;
+}
+
+__device__ __forceinline__ void pair_item(const Fmha2Args& a, long long item, PairItem& c) {
+  const int p_rev = static_cast<int>(item % a.qpairs);
+  long long rest = item / a.qpairs;
+  c.s = static_cast<int>(rest % a.splits);
+  rest /= a.splits;
+  c.h = static_cast<int>(rest % a.heads);
+  c.b = a.order[rest / a.heads];
+  c.q0 = (a.qpairs - 1 - p_rev) * 256;  // later pairs first: they see the most keys when causal
+  c.len = a.lengths[c.b];
+  const int last = min(c.q0 + 256, a.sq) - 1;
+  const int tiles = (visible_upto(last, c.len, a.sq, a.causal) + 127) / 128;
+  c.n_begin = static_cast<int>((long long)tiles * c.s / a.splits);
+  const int n_end = static_cast<int>((long long)tiles * (c.s + 1) / a.splits);
+  c.n = n_end - c.n_begin;
+  const int last_a = min(c.q0 + 128, a.sq) - 1;
+  const int tiles_a = (visible_upto(last_a, c.len, a.sq, a.causal) + 127) / 128;
+  c.n_tile[0] = max(0, min(n_end, tiles_a) - c.n_begin);
+  c.n_tile[1] = (c.q0 + 128 < a.sq) ? c.n : 0;
+}
+
+template <typename T, int NB>
+__global__ void __launch_bounds__(384, 1)
+    fmha2_sm100_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
+                       const __grid_constant__ CUtensorMap vmap, const Fmha2Args a) {
+  using S = Fmha2Shape<NB>;
+  using Tr = ElemTraits<T>;
+  constexpr int BN = S::kBN;
+  constexpr int NS = S::kStages;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* q_smem = smem + S::kQ;
+  uint8_t* k_smem = smem + S::kK;
+  uint8_t* v_smem = smem + S::kV;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::kBar);
+  uint64_t* q_full = bars + 0;
+  uint64_t* q_empty = bars + 1;
+  uint64_t* k_full = bars + 2;
+  uint64_t* k_empty = k_full + NS;
+  uint64_t* v_full = k_empty + NS;
+  uint64_t* v_empty = v_full + NS;
+  uint64_t* s_full = v_empty + NS;  // [2]
+  uint64_t* p_full = s_full + 2;    // [2]
+  uint64_t* pv_done = p_full + 2;   // [2]
+  uint64_t* o_empty = pv_done + 2;  // [2]
+  uint64_t* mma_done = o_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::kTmemSlot);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&p_full[t], 4);   // one arrival per softmax warp
+      mbar_init(&pv_done[t], 1);
+      mbar_init(&o_empty[t], 4);
+    }
+    mbar_init(mma_done, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, S::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before_sync();
+  __syncthreads();
+  tc_fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+  const int grid = gridDim.x;
+  const int D = a.dim;
+
+  if (warp < 4) setmaxnreg_dec_72();  // warpgroup 0 (TMA, MMA, two idle warps) needs few registers
+  if (warp == 0) {
+    // ------------------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&qmap);
+      tma_prefetch_desc(&kmap);
+      tma_prefetch_desc(&vmap);
+      bool ok = true;
+      uint32_t kc = 0, vc = 0, qc = 0;
+      const int boxes = BN / a.box_rows;
+      const uint32_t box_bytes = a.box_rows * 128;
+      auto fail = [&](int site) {
+        ok = false;
+        record_error(a.ws, FGW_ERR_DEVICE_TIMEOUT, site);
+      };
+      for (long long item = blockIdx.x; item < a.items; item += grid) {
+        PairItem c;
+        pair_item(a, item, c);
+        if (c.n <= 0) continue;
+        if (ok && !mbar_wait(q_empty, (qc & 1) ^ 1, a.budget_ns)) fail(40);
+        if (ok) {
+          const int tiles_q = c.n_tile[1] > 0 ? 2 : 1;
+          mbar_arrive_expect_tx(q_full, tiles_q * S::kQBytes);
+          for (int t = 0; t < tiles_q; ++t) {
+            for (int blk = 0; blk < NB; ++blk) {
+              tma_load_4d(q_smem + t * S::kQBytes + blk * S::kTileBytes, &qmap, q_full, blk * 64, c.h,
+                          c.q0 + 128 * t, c.b);
+            }
+          }
+        }
+        ++qc;
+        const int32_t* row_table = a.table + (long long)c.b * a.width;
+        for (int j = 0; j < c.n; ++j) {
+          const int tok0 = (c.n_begin + j) * BN;
+          int nbox = 0;
+          for (int k = 0; k < boxes; ++k) nbox += (tok0 + k * a.box_rows < c.len) ? 1 : 0;
+          // K tile, then V tile of KV step j
+#pragma unroll
+          for (int which = 0; which < 2; ++which) {
+            const uint32_t cnt = which == 0 ? kc : vc;
+            uint64_t* full = which == 0 ? k_full : v_full;
+            uint64_t* empty = which == 0 ? k_empty : v_empty;
+            const CUtensorMap* map = which == 0 ? &kmap : &vmap;
+            uint8_t* ring = which == 0 ? k_smem : v_smem;
+            const int st = cnt % NS;
+            if (ok && !mbar_wait(&empty[st], ((cnt / NS) & 1) ^ 1, a.budget_ns)) fail(41 + which);
+            if (ok) {
+              mbar_arrive_expect_tx(&full[st], NB * nbox * box_bytes);
+              uint8_t* dst = ring + st * S::kKVBytes;
+              for (int k = 0; k < nbox; ++k) {
+                const int tok = tok0 + k * a.box_rows;
+                const int row = row_table[tok / a.page] * a.page + tok % a.page;
+                for (int blk = 0; blk < NB; ++blk) {
+                  tma_load_3d(dst + blk * BN * 128 + k * box_bytes, map, &full[st], blk * 64, c.h, row);
+                }
+              }
+            }
+          }
+          ++kc;
+          ++vc;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------------- UMMA issuer
+    if (lane == 0) {
+      bool ok = true;
+      uint32_t kc = 0, vc = 0, qc = 0;
+      uint32_t pc[2] = {0, 0}, oc[2] = {0, 0};
+      const int fmt = Tr::kUmmaFormat;
+      const uint32_t idesc_qk = umma_idesc_f16(fmt, 128, BN, 0, 0);
+      const uint32_t idesc_pv = umma_idesc_f16(fmt, 128, D, 0, 1);
+      const uint32_t q_base = smem_u32(q_smem);
+      const uint32_t k_base = smem_u32(k_smem);
+      const uint32_t v_base = smem_u32(v_smem);
+      const int ksteps_qk = D / 16;
+      auto wait_or_fail = [&](uint64_t* bar, uint32_t parity, int site) {
+        if (ok && !mbar_wait(bar, parity, a.budget_ns)) {
+          ok = false;
+          record_error(a.ws, FGW_ERR_DEVICE_TIMEOUT, site);
+        }
+        return ok;
+      };
+      // S_t = Q_t K^T into TMEM, K from stage `st` (already waited for).
+      auto qk = [&](int t, int st) {
+        const uint32_t kst = k_base + st * S::kKVBytes;
+        const uint32_t qt = q_base + t * S::kQBytes;
+        for (int kk = 0; kk < ksteps_qk; ++kk) {
+          const uint32_t off = (kk & 3) * 32;
+          const uint64_t adesc = umma_smem_desc(qt + (kk >> 2) * S::kTileBytes + off, 16, 1024, 2);
+          const uint64_t bdesc = umma_smem_desc(kst + (kk >> 2) * BN * 128 + off, 16, 1024, 2);
+          umma_f16_ss(tmem + S::s_col(t), adesc, bdesc, idesc_qk, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[t]);
+      };
+      // O_t += P_t V with P_t read from TMEM (packed into the first 64 columns of S_t).
+      auto pv = [&](int t, int st, bool first) {
+        const uint32_t vst = v_base + st * S::kKVBytes;
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          const uint64_t bdesc = umma_smem_desc(vst + kk * 16 * 128, BN * 128, 1024, 2);
+          umma_f16_ts(tmem + S::o_col(t), tmem + S::s_col(t) + kk * 8, bdesc, idesc_pv, (!first || kk > 0) ? 1u : 0u);
+        }
+      };
+      for (long long item = blockIdx.x; item < a.items; item += grid) {
+        PairItem c;
+        pair_item(a, item, c);
+        if (c.n <= 0) continue;
+        wait_or_fail(q_full, qc & 1, 50);
+        ++qc;
+        // prologue: S_A(0), S_B(0)
+        int kst = kc % NS;
+        if (wait_or_fail(&k_full[kst], (kc / NS) & 1, 51)) {
+          tc_fence_after_sync();
+          for (int t = 0; t < 2; ++t) {
+            if (c.n_tile[t] > 0) qk(t, kst);
+          }
+          umma_commit(&k_empty[kst]);
+        }
+        ++kc;
+        if (c.n == 1 && ok) umma_commit(q_empty);
+        for (int j = 0; j < c.n; ++j) {
+          const int vst = vc % NS;
+          const bool v_ready = wait_or_fail(&v_full[vst], (vc / NS) & 1, 52);
+          ++vc;
+          const bool more = j + 1 < c.n;
+          int knext = kc % NS;
+          bool k_ready = false;
+          for (int t = 0; t < 2; ++t) {
+            if (j < c.n_tile[t]) {
+              bool ready = v_ready && wait_or_fail(&p_full[t], pc[t] & 1, 53 + t);
+              ++pc[t];
+              if (j == 0) ready = ready && wait_or_fail(&o_empty[t], (oc[t] & 1) ^ 1, 55 + t);
+              if (ready) {
+                tc_fence_after_sync();
+                pv(t, vst, j == 0);
+                if (j + 1 == c.n_tile[t]) umma_commit(&pv_done[t]);
+              }
+            }
+            if (t == 1 && ok) umma_commit(&v_empty[vst]);
+            if (more && j + 1 < c.n_tile[t]) {
+              if (!k_ready) k_ready = wait_or_fail(&k_full[knext], (kc / NS) & 1, 57);
+              if (k_ready) {
+                tc_fence_after_sync();
+                qk(t, knext);
+              }
+            }
+          }
+          if (more) {
+            if (ok) umma_commit(&k_empty[knext]);
+            ++kc;
+            if (j + 2 == c.n && ok) umma_commit(q_empty);  // every QK of this item is now issued
+          }
+        }
+        for (int t = 0; t < 2; ++t) {
+          if (c.n_tile[t] > 0) ++oc[t];
+        }
+      }
+      if (ok) {
+        umma_commit(mma_done);
+        mbar_wait(mma_done, 0, a.budget_ns);
+      }
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------------------- softmax / epilogue
+    // Warpgroup 1 (warps 4-7) owns query tile A, warpgroup 2 (warps 8-11) tile B. A warp may only
+    // touch the TMEM lane quarter warp % 4, so each warpgroup covers all 128 rows.
+    setmaxnreg_inc_208();
+    const int t = (warp - 4) / 4;                    // query tile A (0) or B (1)
+    const int row = (warp % 4) * 32 + lane;          // TMEM lane = query row within the tile
+    const uint32_t lane_base = static_cast<uint32_t>((warp % 4) * 32) << 16;
+    const uint32_t s_addr = tmem + lane_base + S::s_col(t);
+    const uint32_t o_addr = tmem + lane_base + S::o_col(t);
+    bool ok = true;
+    uint32_t sc = 0, pd = 0, vbase = 0;
+    auto wait_warp = [&](uint64_t* bar, uint32_t parity, int site) {
+      if (ok) {
+        ok = __all_sync(0xffffffffu, mbar_wait(bar, parity, a.budget_ns));
+        if (!ok && lane == 0) record_error(a.ws, FGW_ERR_DEVICE_TIMEOUT, site);
+      }
+      return ok;
+    };
+    for (long long item = blockIdx.x; item < a.items; item += grid) {
+      PairItem c;
+      pair_item(a, item, c);
+      const int q = c.q0 + 128 * t + row;
+      const bool row_valid = q < a.sq;
+      const int vis = row_valid ? visible_upto(q, c.len, a.sq, a.causal) : 0;
+      const int n_t = t == 0 ? c.n_tile[0] : c.n_tile[1];
+      float m = -INFINITY, l = 0.f;
+      for (int j = 0; j < n_t; ++j) {
+        const int tok0 = (c.n_begin + j) * BN;
+        wait_warp(&s_full[t], sc & 1, 60 + t);
+        ++sc;
+        const int valid_cols = min(max(vis - tok0, 0), BN);
+        const bool tail = valid_cols < BN;  // masking only on tail / diagonal tiles
+        // The whole S row in registers with one wait.
+        uint32_t sr[BN];
+        if (ok) {
+          tc_fence_after_sync();
+#pragma unroll
+          for (int cb = 0; cb < BN / 32; ++cb) {
+            tmem_ld32(s_addr + cb * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[cb * 32]));
+          }
+          tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int i = 0; i < BN; ++i) sr[i] = __float_as_uint(-INFINITY);
+        }
+        if (tail) {
+          // ragged / diagonal tile: mask columns at or past this row's visible count
+#pragma unroll
+          for (int col = 0; col < BN; ++col) {
+            if (col >= valid_cols) sr[col] = 0xff800000u;  // -inf
+          }
+        }
+        auto sval = [&](int col) -> float { return __uint_as_float(sr[col]); };
+        float mx_raw = -INFINITY;
+#pragma unroll
+        for (int col = 0; col < BN; col += 4) {
+          mx_raw = fmaxf(mx_raw, fmaxf(fmaxf(sval(col), sval(col + 1)), fmaxf(sval(col + 2), sval(col + 3))));
+        }
+        const float mx = mx_raw * a.scale_log2;  // scale > 0; -inf stays -inf
+        float m_new = m;
+        bool grow = false;
+        if (j == 0) {
+          m_new = mx;
+        } else if (mx > m + 8.0f) {
+          grow = true;
+        }
+        const bool warp_grow = __any_sync(0xffffffffu, grow);
+        float alpha = 1.f;
+        if (warp_grow && j > 0) {
+          m_new = fmaxf(m, mx);
+          alpha = (m == -INFINITY) ? 0.f : fast_exp2(m - m_new);
+          if (ok) {
+            // The commit that published S_t(j) also covers PV_t(j-1): O_t is stable.
+            for (int cb = 0; cb < D / 16; ++cb) {
+              uint32_t r[16];
+              tmem_ld16(o_addr + cb * 16, r);
+              tmem_wait_ld();
+#pragma unroll
+              for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+              tmem_st16(o_addr + cb * 16, r);
+            }
+          }
+        }
+        const float neg_m = (m_new == -INFINITY) ? 0.f : -m_new;
+        // P = 2^(s*scale - m): two FP32 lanes per instruction; on full tiles one pair in four goes
+        // through the FMA-pipe polynomial instead of the SFU (the two pipes run in parallel). Packed 16-bit pairs overwrite the first
+        // 64 S columns (the whole row is already in registers).
+        float rowsum = 0.f;
+        if (ok) {
+          const float2 scale2 = make_float2(a.scale_log2, a.scale_log2);
+          const float2 negm2 = make_float2(neg_m, neg_m);
+          float2 sum2 = make_float2(0.f, 0.f);
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            uint32_t packed[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const int col = half * 64 + 2 * i;
+              const float2 x = __ffma2_rn(make_float2(sval(col), sval(col + 1)), scale2, negm2);
+              float2 p;
+              if (!tail && (i % 4) == 3) {
+                p = poly_exp2_pair(x);
+              } else {
+                p = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+              }
+              sum2 = __fadd2_rn(sum2, p);
+              packed[i] = Tr::pack2(p.x, p.y);
+            }
+            tmem_st32(s_addr + half * 32, packed);
+          }
+          tmem_wait_st();
+          rowsum = sum2.x + sum2.y;
+        }
+        // Value rows past the cache end: the first tile to use this V stage zeroes them.
+        const bool mine = (t == 0) ? true : (j >= c.n_tile[0]);
+        if (tok0 + BN > c.len && mine) {
+          const uint32_t vcount = vbase + j;
+          const int vst = vcount % NS;
+          wait_warp(&v_full[vst], (vcount / NS) & 1, 62);
+          if (ok && tok0 + row >= c.len) {
+            uint8_t* vrow = v_smem + vst * S::kKVBytes + row * 128;
+#pragma unroll
+            for (int blk = 0; blk < NB; ++blk) {
+#pragma unroll
+              for (int ch = 0; ch < 8; ++ch) {
+                *reinterpret_cast<uint4*>(vrow + blk * BN * 128 + ch * 16) = make_uint4(0, 0, 0, 0);
+              }
+            }
+          }
+          fence_proxy_async_smem();
+        }
+        tc_fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[t]);
+        l = l * alpha + rowsum;
+        m = m_new;
+      }
+      if (c.n > 0) vbase += c.n;
+      // epilogue
+      float inv = 0.f;
+      if (n_t > 0) {
+        wait_warp(&pv_done[t], pd & 1, 63);
+        ++pd;
+        inv = l > 0.f ? 1.f / l : 0.f;
+        if (ok) tc_fence_after_sync();
+      }
+      const long long row_id = row_valid ? ((long long)c.b * a.sq + q) * a.heads + c.h : 0;
+      for (int cb = 0; cb < D / 16; ++cb) {
+        float o[16];
+        if (n_t > 0 && ok) {
+          uint32_t r[16];
+          tmem_ld16(o_addr + cb * 16, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) o[i] = __uint_as_float(r[i]) * inv;
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) o[i] = 0.f;
+        }
+        if (!row_valid) continue;
+        if (a.write_partials) {
+          float4* dst = reinterpret_cast<float4*>(a.part_o + (row_id * a.splits + c.s) * D + cb * 16);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) dst[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+        } else {
+          uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<T*>(a.out) + row_id * D + cb * 16);
+          dst[0] = make_uint4(Tr::pack2(o[0], o[1]), Tr::pack2(o[2], o[3]), Tr::pack2(o[4], o[5]),
+                              Tr::pack2(o[6], o[7]));
+          dst[1] = make_uint4(Tr::pack2(o[8], o[9]), Tr::pack2(o[10], o[11]), Tr::pack2(o[12], o[13]),
+                              Tr::pack2(o[14], o[15]));
+        }
+      }
+      if (row_valid && a.write_partials) {
+        a.part_lse[row_id * a.splits + c.s] = (n_t > 0 && l > 0.f) ? m + fast_log2(l) : kEmptyLse;
+      }
+      if (n_t > 0) {
+        tc_fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&o_empty[t]);
+      }
+    }
+  }
+  tc_fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after_sync();
+    tmem_dealloc(tmem, S::kTmemCols);
+  }
+}
+
+template <typename T, int NB>
+static cudaError_t launch_fmha2_t(const LaunchDesc& d, const Fmha2Args& args, const CUtensorMap& qmap,
+                                  const CUtensorMap& kmap, const CUtensorMap& vmap) {
+  using S = Fmha2Shape<NB>;
+  auto kernel = fmha2_sm100_kernel<T, NB>;
+  // setmaxnreg.inc only succeeds if the registers the block was launched with cover the new split:
+  // warpgroup 0 drops to 72 per thread, the two softmax warpgroups rise to 208 per thread. Refuse to
+  // launch a build whose allocation would not cover that (the increase would otherwise never complete).
+  cudaFuncAttributes attr;
+  cudaError_t err = cudaFuncGetAttributes(&attr, kernel);
+  if (err != cudaSuccess) return err;
+  const int allocated = ((attr.numRegs + 7) / 8) * 8 * S::kThreads;
+  if (allocated < 4 * 32 * 72 + 8 * 32 * 208) return cudaErrorNotSupported;
+  err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kBytes);
+  if (err != cudaSuccess) return err;
+  const long long cap = d.p.grid_cap > 0 ? d.p.grid_cap : d.sm_count;
+  const long long grid = std::min<long long>(args.items, std::min<long long>(cap, d.sm_count));
+  if (grid <= 0) return cudaSuccess;
+  kernel<<<(unsigned)grid, S::kThreads, S::kBytes, d.stream>>>(qmap, kmap, vmap, args);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_tensor_pairs(const LaunchDesc& d, bool write_partials, const CUtensorMap& qmap,
+                                const CUtensorMap& kmap, const CUtensorMap& vmap, int box_rows) {
+  const fgw_mha_params& p = d.p;
+  Fmha2Args args;
+  args.out = p.out;
+  args.table = p.block_table;
+  args.lengths = d.lens;
+  args.order = d.order;
+  args.part_o = d.part_o;
+  args.part_lse = d.part_lse;
+  args.ws = d.header;
+  args.batch = p.batch;
+  args.sq = p.q_len;
+  args.heads = p.heads;
+  args.dim = p.head_dim;
+  args.width = p.table_width;
+  args.page = p.page_size;
+  args.splits = p.num_splits;
+  args.causal = p.causal;
+  args.box_rows = box_rows;
+  args.write_partials = write_partials ? 1 : 0;
+  args.qpairs = (p.q_len + 255) / 256;
+  args.items = (long long)p.batch * p.heads * p.num_splits * args.qpairs;
+  args.scale_log2 = (1.0f / sqrtf((float)p.head_dim)) * kLog2e;
+  args.budget_ns = d.budget_ns;
+  const bool bf16 = p.dtype == FGW_DTYPE_BFLOAT16;
+  if (p.head_dim <= 64) {
+    return bf16 ? launch_fmha2_t<__nv_bfloat16, 1>(d, args, qmap, kmap, vmap)
+                : launch_fmha2_t<__half, 1>(d, args, qmap, kmap, vmap);
+  }
+  if (p.head_dim <= 128) {
+    return bf16 ? launch_fmha2_t<__nv_bfloat16, 2>(d, args, qmap, kmap, vmap)
+                : launch_fmha2_t<__half, 2>(d, args, qmap, kmap, vmap);
+  }
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace fgw

@@ -22,6 +22,7 @@ struct LaunchDesc {
   float* part_lse;    // [batch*q_len*heads, splits] base-2 LSE per partial
   uint64_t budget_ns;
   int sm_count;
+  bool single_tile;   // force the one-query-tile tensor kernel (FGW_MHA_TENSOR_SINGLE_TILE set)
   cudaStream_t stream;
 };
 
@@ -34,6 +35,9 @@ cudaError_t launch_plan(const LaunchDesc& d);
 cudaError_t launch_decode(const LaunchDesc& d, bool write_partials);
 cudaError_t launch_merge(const LaunchDesc& d);
 cudaError_t launch_tensor(const LaunchDesc& d, bool write_partials);
+// Two-query-tile tensor kernel (head_dim <= 128); called by launch_tensor with its tensor maps.
+cudaError_t launch_tensor_pairs(const LaunchDesc& d, bool write_partials, const CUtensorMap& qmap,
+                                const CUtensorMap& kmap, const CUtensorMap& vmap, int box_rows);
 
 // Which path AUTO picks.
 int resolve_path(const fgw_mha_params& p);
