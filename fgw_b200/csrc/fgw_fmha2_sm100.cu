@@ -393,14 +393,15 @@ __global__ void __launch_bounds__(384, 1)
           }
         }
         const float neg_m = (m_new == -INFINITY) ? 0.f : -m_new;
-        // P = 2^(s*scale - m): two FP32 lanes per instruction; on full tiles one pair in four goes
-        // through the FMA-pipe polynomial instead of the SFU (the two pipes run in parallel). Packed 16-bit pairs overwrite the first
-        // 64 S columns (the whole row is already in registers).
+        // P = 2^(s*scale - m) on the SFU, scale-and-subtract two FP32 lanes per instruction; the packed
+        // 16-bit pairs overwrite the first 64 S columns (the whole row is already in registers).
         float rowsum = 0.f;
         if (ok) {
           const float2 scale2 = make_float2(a.scale_log2, a.scale_log2);
           const float2 negm2 = make_float2(neg_m, neg_m);
-          float2 sum2 = make_float2(0.f, 0.f);
+          // four independent partial sums keep the add chain short
+          float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                           make_float2(0.f, 0.f)};
 #pragma unroll
           for (int half = 0; half < 2; ++half) {
             uint32_t packed[32];
@@ -408,19 +409,14 @@ __global__ void __launch_bounds__(384, 1)
             for (int i = 0; i < 32; ++i) {
               const int col = half * 64 + 2 * i;
               const float2 x = __ffma2_rn(make_float2(sval(col), sval(col + 1)), scale2, negm2);
-              float2 p;
-              if (!tail && (i % 4) == 3) {
-                p = poly_exp2_pair(x);
-              } else {
-                p = make_float2(fast_exp2(x.x), fast_exp2(x.y));
-              }
-              sum2 = __fadd2_rn(sum2, p);
+              const float2 p = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+              acc[i % 4] = __fadd2_rn(acc[i % 4], p);
               packed[i] = Tr::pack2(p.x, p.y);
             }
             tmem_st32(s_addr + half * 32, packed);
           }
           tmem_wait_st();
-          rowsum = sum2.x + sum2.y;
+          rowsum = (acc[0].x + acc[0].y) + (acc[1].x + acc[1].y) + (acc[2].x + acc[2].y) + (acc[3].x + acc[3].y);
         }
         // Value rows past the cache end: the first tile to use this V stage zeroes them.
         const bool mine = (t == 0) ? true : (j >= c.n_tile[0]);
