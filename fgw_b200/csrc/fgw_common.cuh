@@ -98,6 +98,44 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64
   }
 }
 
+// Non-blocking test of one phase.
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// Waits until every listed phase has completed (a null barrier counts as complete). Each round tests all
+// pending barriers back to back, so the round trips of independent barriers overlap instead of adding up
+// (a single mbarrier test costs on the order of a couple of hundred cycles). Returns false if the budget
+// ran out first.
+__device__ __forceinline__ bool mbar_wait_all(uint64_t* b0, uint32_t p0, uint64_t* b1, uint32_t p1, uint64_t* b2,
+                                              uint32_t p2, uint64_t* b3, uint32_t p3, uint64_t budget_ns) {
+  bool d0 = b0 == nullptr, d1 = b1 == nullptr, d2 = b2 == nullptr, d3 = b3 == nullptr;
+  uint64_t start = 0;
+  for (uint32_t round = 0;; ++round) {
+    if (!d0) d0 = mbar_test_wait(b0, p0);
+    if (!d1) d1 = mbar_test_wait(b1, p1);
+    if (!d2) d2 = mbar_test_wait(b2, p2);
+    if (!d3) d3 = mbar_test_wait(b3, p3);
+    if (d0 && d1 && d2 && d3) return true;
+    if ((round & 31) == 0) {
+      const uint64_t now = global_timer_ns();
+      if (round == 0) {
+        start = now;
+      } else if (now - start > budget_ns) {
+        return false;
+      }
+    }
+  }
+}
+
 // Named barrier over a subset of warps (id 0 is __syncthreads).
 __device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
@@ -206,8 +244,15 @@ __device__ __forceinline__ float2 poly_exp2_pair(float2 x) {
   return make_float2(__int_as_float(bx), __int_as_float(by));
 }
 
-__device__ __forceinline__ void setmaxnreg_dec_72() { asm volatile("setmaxnreg.dec.sync.aligned.u32 72;" ::: "memory"); }
-__device__ __forceinline__ void setmaxnreg_inc_208() { asm volatile("setmaxnreg.inc.sync.aligned.u32 208;" ::: "memory"); }
+// Per-warpgroup register budgets (setmaxnreg); N is a multiple of 8 in [24, 256].
+template <int N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N) : "memory");
+}
+template <int N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N) : "memory");
+}
 
 __device__ __forceinline__ float fast_log2(float x) {
   float y;
@@ -260,6 +305,31 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
       "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// The same two UMMA forms with each shared-memory descriptor passed as its two 32-bit words (see
+// umma_desc_lo / umma_desc_hi), so an issue loop only adds an offset to the low word per instruction.
+__device__ __forceinline__ void umma_f16_ss_w(uint32_t d_tmem, uint32_t a_lo, uint32_t a_hi, uint32_t b_lo,
+                                              uint32_t b_hi, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b64 da, db;\n\t"
+      "mov.b64 da, {%1, %2};\n\t"
+      "mov.b64 db, {%3, %4};\n\t"
+      "setp.ne.b32 p, %6, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %5, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_lo), "r"(a_hi), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_f16_ts_w(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_lo, uint32_t b_hi,
+                                              uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b64 db;\n\t"
+      "mov.b64 db, {%2, %3};\n\t"
+      "setp.ne.b32 p, %5, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], db, %4, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 
@@ -319,6 +389,18 @@ __device__ __forceinline__ uint64_t umma_smem_desc(uint32_t start, uint32_t lbo,
   d |= static_cast<uint64_t>(1) << 46;  // descriptor version for SM100
   d |= static_cast<uint64_t>(swizzle & 0x7u) << 61;
   return d;
+}
+
+// The two 32-bit words of umma_smem_desc. Low word: start address >> 4 (bits 0-13) and leading byte
+// offset >> 4 (bits 16-29). High word: stride byte offset >> 4 (bits 0-13), descriptor version 1 (bit 14)
+// and the swizzle mode (bits 29-31). Adding (byte offset >> 4) to the low word moves the start address;
+// shared-memory addresses stay below 2^18, so the sum never carries into the leading-offset field.
+__device__ __forceinline__ uint32_t umma_desc_lo(uint32_t start, uint32_t lbo) {
+  return ((start >> 4) & 0x3FFFu) | (((lbo >> 4) & 0x3FFFu) << 16);
+}
+
+__host__ __device__ constexpr uint32_t umma_desc_hi(uint32_t sbo, uint32_t swizzle) {
+  return ((sbo >> 4) & 0x3FFFu) | (1u << 14) | ((swizzle & 0x7u) << 29);
 }
 
 // Instruction descriptor for kind::f16 with FP32 accumulation.

@@ -43,6 +43,9 @@ struct Fmha2Shape {
   static constexpr int kKVBytes = NB * kBN * 128;        // one K (or V) stage
   static constexpr int kStages = NB == 1 ? 4 : 2;
   static constexpr int kThreads = 384;
+  // registers per thread after the warpgroup split (4 x 32 x 88 + 8 x 32 x 208 = 384 x 168)
+  static constexpr int kRegsControl = 88;
+  static constexpr int kRegsSoftmax = 208;
   // TMEM column of S_t / O_t for query tile t
   __device__ __forceinline__ static uint32_t s_col(int t) { return static_cast<uint32_t>(t) * 128u; }
   __device__ __forceinline__ static uint32_t o_col(int t) { return 256u + static_cast<uint32_t>(t) * 128u; }
@@ -85,6 +88,27 @@ __device__ __forceinline__ void pair_item(const Fmha2Args& a, long long item, Pa
   const int tiles_a = (visible_upto(last_a, c.len, a.sq, a.causal) + 127) / 128;
   c.n_tile[0] = max(0, min(n_end, tiles_a) - c.n_begin);
   c.n_tile[1] = (c.q0 + 128 < a.sq) ? c.n : 0;
+}
+
+// 2^(s * scale - m) for 64 consecutive scores (32 FP32 pairs, scale-and-subtract two lanes per
+// instruction), summed into four independent partial sums and packed to 16-bit pairs. With kFmaPipe, one
+// pair in four is evaluated by poly_exp2_pair on the FMA pipe so that the SFU and FMA pipes share the
+// work; only used on tiles without masked (-inf) scores, since poly_exp2_pair clamps its input.
+template <typename Tr, bool kFmaPipe>
+__device__ __forceinline__ void exp2_pack_half(const uint32_t* sr, float2 scale2, float2 negm2, float2 (&acc)[4],
+                                               uint32_t (&packed)[32]) {
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const float2 x = __ffma2_rn(make_float2(__uint_as_float(sr[2 * i]), __uint_as_float(sr[2 * i + 1])), scale2, negm2);
+    float2 p;
+    if (kFmaPipe && (i % 4) == 3) {
+      p = poly_exp2_pair(x);
+    } else {
+      p = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+    }
+    acc[i % 4] = __fadd2_rn(acc[i % 4], p);
+    packed[i] = Tr::pack2(p.x, p.y);
+  }
 }
 
 template <typename T, int NB>
@@ -146,7 +170,7 @@ __global__ void __launch_bounds__(384, 1)
   const int grid = gridDim.x;
   const int D = a.dim;
 
-  if (warp < 4) setmaxnreg_dec_72();  // warpgroup 0 (TMA, MMA, two idle warps) needs few registers
+  if (warp < 4) setmaxnreg_dec<S::kRegsControl>();  // warpgroup 0: TMA, MMA and two idle warps
   if (warp == 0) {
     // ------------------------------------------------------------------------- TMA producer
     if (lane == 0) {
@@ -218,9 +242,11 @@ __global__ void __launch_bounds__(384, 1)
       const int fmt = Tr::kUmmaFormat;
       const uint32_t idesc_qk = umma_idesc_f16(fmt, 128, BN, 0, 0);
       const uint32_t idesc_pv = umma_idesc_f16(fmt, 128, D, 0, 1);
-      const uint32_t q_base = smem_u32(q_smem);
-      const uint32_t k_base = smem_u32(k_smem);
-      const uint32_t v_base = smem_u32(v_smem);
+      // Descriptor words: each issue below only adds a constant to a low word.
+      uint32_t q_lo = umma_desc_lo(smem_u32(q_smem), 16);
+      uint32_t k_lo = umma_desc_lo(smem_u32(k_smem), 16);
+      uint32_t v_lo = umma_desc_lo(smem_u32(v_smem), BN * 128);
+      constexpr uint32_t kHi = umma_desc_hi(1024, 2);
       const int ksteps_qk = D / 16;
       auto wait_or_fail = [&](uint64_t* bar, uint32_t parity, int site) {
         if (ok && !mbar_wait(bar, parity, a.budget_ns)) {
@@ -229,70 +255,87 @@ __global__ void __launch_bounds__(384, 1)
         }
         return ok;
       };
+      // Several phases at once (null entries are skipped): one polling loop instead of a chain of waits.
+      auto wait_all_or_fail = [&](uint64_t* b0, uint32_t p0, uint64_t* b1, uint32_t p1, uint64_t* b2, uint32_t p2,
+                                  uint64_t* b3, uint32_t p3, int site) {
+        if (ok && !mbar_wait_all(b0, p0, b1, p1, b2, p2, b3, p3, a.budget_ns)) {
+          ok = false;
+          record_error(a.ws, FGW_ERR_DEVICE_TIMEOUT, site);
+        }
+        return ok;
+      };
       // S_t = Q_t K^T into TMEM, K from stage `st` (already waited for).
       auto qk = [&](int t, int st) {
-        const uint32_t kst = k_base + st * S::kKVBytes;
-        const uint32_t qt = q_base + t * S::kQBytes;
-        for (int kk = 0; kk < ksteps_qk; ++kk) {
-          const uint32_t off = (kk & 3) * 32;
-          const uint64_t adesc = umma_smem_desc(qt + (kk >> 2) * S::kTileBytes + off, 16, 1024, 2);
-          const uint64_t bdesc = umma_smem_desc(kst + (kk >> 2) * BN * 128 + off, 16, 1024, 2);
-          umma_f16_ss(tmem + S::s_col(t), adesc, bdesc, idesc_qk, kk > 0 ? 1u : 0u);
+        const uint32_t a_lo = q_lo + static_cast<uint32_t>((t * S::kQBytes) >> 4);
+        const uint32_t b_lo = k_lo + static_cast<uint32_t>((st * S::kKVBytes) >> 4);
+#pragma unroll
+        for (int kk = 0; kk < 4 * NB; ++kk) {
+          if (kk < ksteps_qk) {
+            umma_f16_ss_w(tmem + S::s_col(t), a_lo + (((kk >> 2) * S::kTileBytes + (kk & 3) * 32) >> 4), kHi,
+                          b_lo + (((kk >> 2) * BN * 128 + (kk & 3) * 32) >> 4), kHi, idesc_qk, kk > 0 ? 1u : 0u);
+          }
         }
         umma_commit(&s_full[t]);
       };
-      // O_t += P_t V with P_t read from TMEM (packed into the first 64 columns of S_t).
+      // O_t += P_t V: P_t read from TMEM (packed into the first 64 columns of S_t), V from stage `st`.
       auto pv = [&](int t, int st, bool first) {
-        const uint32_t vst = v_base + st * S::kKVBytes;
+        const uint32_t b_lo = v_lo + static_cast<uint32_t>((st * S::kKVBytes) >> 4);
+#pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
-          const uint64_t bdesc = umma_smem_desc(vst + kk * 16 * 128, BN * 128, 1024, 2);
-          umma_f16_ts(tmem + S::o_col(t), tmem + S::s_col(t) + kk * 8, bdesc, idesc_pv, (!first || kk > 0) ? 1u : 0u);
+          umma_f16_ts_w(tmem + S::o_col(t), tmem + S::s_col(t) + kk * 8, b_lo + ((kk * 16 * 128) >> 4), kHi, idesc_pv,
+                        (!first || kk > 0) ? 1u : 0u);
         }
       };
       for (long long item = blockIdx.x; item < a.items; item += grid) {
         PairItem c;
         pair_item(a, item, c);
         if (c.n <= 0) continue;
-        wait_or_fail(q_full, qc & 1, 50);
-        ++qc;
-        // prologue: S_A(0), S_B(0)
+        // prologue: S_A(0), S_B(0) once Q and K(0) are in
         int kst = kc % NS;
-        if (wait_or_fail(&k_full[kst], (kc / NS) & 1, 51)) {
+        if (wait_all_or_fail(q_full, qc & 1, &k_full[kst], (kc / NS) & 1, nullptr, 0, nullptr, 0, 50)) {
           tc_fence_after_sync();
           for (int t = 0; t < 2; ++t) {
             if (c.n_tile[t] > 0) qk(t, kst);
           }
           umma_commit(&k_empty[kst]);
         }
+        ++qc;
         ++kc;
         if (c.n == 1 && ok) umma_commit(q_empty);
         for (int j = 0; j < c.n; ++j) {
+          // Opaque to the compiler, so the descriptor sums are formed where they are used instead of being
+          // hoisted out of the loops (which would keep one register per stage and step live).
+          asm volatile("" : "+r"(q_lo), "+r"(k_lo), "+r"(v_lo));
           const int vst = vc % NS;
-          const bool v_ready = wait_or_fail(&v_full[vst], (vc / NS) & 1, 52);
+          const uint32_t v_par = (vc / NS) & 1;
           ++vc;
           const bool more = j + 1 < c.n;
-          int knext = kc % NS;
-          bool k_ready = false;
+          const int knext = kc % NS;
+          const uint32_t k_par = (kc / NS) & 1;
+          bool v_seen = false, k_seen = !more;
           for (int t = 0; t < 2; ++t) {
-            if (j < c.n_tile[t]) {
-              bool ready = v_ready && wait_or_fail(&p_full[t], pc[t] & 1, 53 + t);
-              ++pc[t];
-              if (j == 0) ready = ready && wait_or_fail(&o_empty[t], (oc[t] & 1) ^ 1, 55 + t);
+            const bool pv_t = j < c.n_tile[t];
+            const bool qk_t = more && j + 1 < c.n_tile[t];
+            if (pv_t || qk_t) {
+              // this tile's P, the V tile, the next K tile and (first tile of an item) an empty O, in one poll
+              const bool ready = wait_all_or_fail(pv_t ? &p_full[t] : nullptr, pc[t] & 1,
+                                                  (pv_t && !v_seen) ? &v_full[vst] : nullptr, v_par,
+                                                  (qk_t && !k_seen) ? &k_full[knext] : nullptr, k_par,
+                                                  (pv_t && j == 0) ? &o_empty[t] : nullptr, (oc[t] & 1) ^ 1, 53 + t);
+              v_seen = v_seen || pv_t;
+              k_seen = k_seen || qk_t;
               if (ready) {
                 tc_fence_after_sync();
-                pv(t, vst, j == 0);
-                if (j + 1 == c.n_tile[t]) umma_commit(&pv_done[t]);
+                if (pv_t) {
+                  pv(t, vst, j == 0);
+                  if (j + 1 == c.n_tile[t]) umma_commit(&pv_done[t]);
+                }
+                if (qk_t) qk(t, knext);
               }
             }
-            if (t == 1 && ok) umma_commit(&v_empty[vst]);
-            if (more && j + 1 < c.n_tile[t]) {
-              if (!k_ready) k_ready = wait_or_fail(&k_full[knext], (kc / NS) & 1, 57);
-              if (k_ready) {
-                tc_fence_after_sync();
-                qk(t, knext);
-              }
-            }
+            if (pv_t) ++pc[t];
           }
+          if (ok) umma_commit(&v_empty[vst]);
           if (more) {
             if (ok) umma_commit(&k_empty[knext]);
             ++kc;
@@ -312,7 +355,7 @@ __global__ void __launch_bounds__(384, 1)
     // ------------------------------------------------------------------------- softmax / epilogue
     // Warpgroup 1 (warps 4-7) owns query tile A, warpgroup 2 (warps 8-11) tile B. A warp may only
     // touch the TMEM lane quarter warp % 4, so each warpgroup covers all 128 rows.
-    setmaxnreg_inc_208();
+    setmaxnreg_inc<S::kRegsSoftmax>();
     const int t = (warp - 4) / 4;                    // query tile A (0) or B (1)
     const int row = (warp % 4) * 32 + lane;          // TMEM lane = query row within the tile
     const uint32_t lane_base = static_cast<uint32_t>((warp % 4) * 32) << 16;
@@ -393,8 +436,8 @@ __global__ void __launch_bounds__(384, 1)
           }
         }
         const float neg_m = (m_new == -INFINITY) ? 0.f : -m_new;
-        // P = 2^(s*scale - m) on the SFU, scale-and-subtract two FP32 lanes per instruction; the packed
-        // 16-bit pairs overwrite the first 64 S columns (the whole row is already in registers).
+        // P = 2^(s*scale - m): the packed 16-bit pairs overwrite the first 64 S columns (the whole row is
+        // already in registers).
         float rowsum = 0.f;
         if (ok) {
           const float2 scale2 = make_float2(a.scale_log2, a.scale_log2);
@@ -405,20 +448,14 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll
           for (int half = 0; half < 2; ++half) {
             uint32_t packed[32];
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const int col = half * 64 + 2 * i;
-              const float2 x = __ffma2_rn(make_float2(sval(col), sval(col + 1)), scale2, negm2);
-              const float2 p = make_float2(fast_exp2(x.x), fast_exp2(x.y));
-              acc[i % 4] = __fadd2_rn(acc[i % 4], p);
-              packed[i] = Tr::pack2(p.x, p.y);
-            }
+            exp2_pack_half<Tr, false>(&sr[half * 64], scale2, negm2, acc, packed);
             tmem_st32(s_addr + half * 32, packed);
           }
           tmem_wait_st();
           rowsum = (acc[0].x + acc[0].y) + (acc[1].x + acc[1].y) + (acc[2].x + acc[2].y) + (acc[3].x + acc[3].y);
         }
-        // Value rows past the cache end: the first tile to use this V stage zeroes them.
+        // Value rows past the cache end: the first tile to use this V stage zeroes them before it
+        // releases P (the PV reads them).
         const bool mine = (t == 0) ? true : (j >= c.n_tile[0]);
         if (tok0 + BN > c.len && mine) {
           const uint32_t vcount = vbase + j;
@@ -501,13 +538,13 @@ static cudaError_t launch_fmha2_t(const LaunchDesc& d, const Fmha2Args& args, co
   using S = Fmha2Shape<NB>;
   auto kernel = fmha2_sm100_kernel<T, NB>;
   // setmaxnreg.inc only succeeds if the registers the block was launched with cover the new split:
-  // warpgroup 0 drops to 72 per thread, the two softmax warpgroups rise to 208 per thread. Refuse to
-  // launch a build whose allocation would not cover that (the increase would otherwise never complete).
+  // warpgroup 0 drops to kRegsControl per thread, the two softmax warpgroups rise to kRegsSoftmax. Refuse
+  // to launch a build whose allocation would not cover that (the increase would otherwise never complete).
   cudaFuncAttributes attr;
   cudaError_t err = cudaFuncGetAttributes(&attr, kernel);
   if (err != cudaSuccess) return err;
   const int allocated = ((attr.numRegs + 7) / 8) * 8 * S::kThreads;
-  if (allocated < 4 * 32 * 72 + 8 * 32 * 208) return cudaErrorNotSupported;
+  if (allocated < 4 * 32 * S::kRegsControl + 8 * 32 * S::kRegsSoftmax) return cudaErrorNotSupported;
   err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kBytes);
   if (err != cudaSuccess) return err;
   const long long cap = d.p.grid_cap > 0 ? d.p.grid_cap : d.sm_count;
