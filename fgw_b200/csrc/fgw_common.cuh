@@ -125,9 +125,10 @@ __device__ __forceinline__ bool mbar_wait_all(uint64_t* b0, uint32_t p0, uint64_
     if (!d2) d2 = mbar_test_wait(b2, p2);
     if (!d3) d3 = mbar_test_wait(b3, p3);
     if (d0 && d1 && d2 && d3) return true;
-    if ((round & 31) == 0) {
+    // the clock is read only once the wait has lasted a while (reading it costs hundreds of cycles)
+    if ((round & 31) == 31) {
       const uint64_t now = global_timer_ns();
-      if (round == 0) {
+      if (round == 31) {
         start = now;
       } else if (now - start > budget_ns) {
         return false;

@@ -46,6 +46,8 @@ struct Fmha2Shape {
   // registers per thread after the warpgroup split (4 x 32 x 88 + 8 x 32 x 208 = 384 x 168)
   static constexpr int kRegsControl = 88;
   static constexpr int kRegsSoftmax = 208;
+  // full tiles evaluate one exponential pair in kFmaEvery on the FMA pipe (0: all on the SFU)
+  static constexpr int kFmaEvery = 0;
   // TMEM column of S_t / O_t for query tile t
   __device__ __forceinline__ static uint32_t s_col(int t) { return static_cast<uint32_t>(t) * 128u; }
   __device__ __forceinline__ static uint32_t o_col(int t) { return 256u + static_cast<uint32_t>(t) * 128u; }
@@ -91,17 +93,17 @@ __device__ __forceinline__ void pair_item(const Fmha2Args& a, long long item, Pa
 }
 
 // 2^(s * scale - m) for 64 consecutive scores (32 FP32 pairs, scale-and-subtract two lanes per
-// instruction), summed into four independent partial sums and packed to 16-bit pairs. With kFmaPipe, one
-// pair in four is evaluated by poly_exp2_pair on the FMA pipe so that the SFU and FMA pipes share the
+// instruction), summed into four independent partial sums and packed to 16-bit pairs. With kFmaEvery = k > 0,
+// one pair in k is evaluated by poly_exp2_pair on the FMA pipe so that the SFU and FMA pipes share the
 // work; only used on tiles without masked (-inf) scores, since poly_exp2_pair clamps its input.
-template <typename Tr, bool kFmaPipe>
+template <typename Tr, int kFmaEvery>
 __device__ __forceinline__ void exp2_pack_half(const uint32_t* sr, float2 scale2, float2 negm2, float2 (&acc)[4],
                                                uint32_t (&packed)[32]) {
 #pragma unroll
   for (int i = 0; i < 32; ++i) {
     const float2 x = __ffma2_rn(make_float2(__uint_as_float(sr[2 * i]), __uint_as_float(sr[2 * i + 1])), scale2, negm2);
     float2 p;
-    if (kFmaPipe && (i % 4) == 3) {
+    if (kFmaEvery > 0 && (i % (kFmaEvery > 0 ? kFmaEvery : 1)) == kFmaEvery - 1) {
       p = poly_exp2_pair(x);
     } else {
       p = make_float2(fast_exp2(x.x), fast_exp2(x.y));
@@ -448,7 +450,11 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll
           for (int half = 0; half < 2; ++half) {
             uint32_t packed[32];
-            exp2_pack_half<Tr, false>(&sr[half * 64], scale2, negm2, acc, packed);
+            if (tail) {
+              exp2_pack_half<Tr, 0>(&sr[half * 64], scale2, negm2, acc, packed);
+            } else {
+              exp2_pack_half<Tr, S::kFmaEvery>(&sr[half * 64], scale2, negm2, acc, packed);
+            }
             tmem_st32(s_addr + half * 32, packed);
           }
           tmem_wait_st();
