@@ -25,6 +25,13 @@ PATH_AUTO = 0
 PATH_DECODE = 1
 PATH_TENSOR = 2
 
+# fgw_schedule
+SCHEDULE_AUTO = 0
+SCHEDULE_STRIDED = 1
+SCHEDULE_CONTIGUOUS = 2
+
+ABI_VERSION = 2  # FGW_MHA_ABI_VERSION the Params layout below matches
+
 EXPORTED = (
     "fgw_mha_abi_version",
     "fgw_mha_status_string",
@@ -78,7 +85,8 @@ class Params(ctypes.Structure):
         ("grid_cap", ctypes.c_int32),
         ("path", ctypes.c_int32),
         ("wait_budget_ms", ctypes.c_int32),
-        ("reserved", ctypes.c_int32 * 4),
+        ("schedule", ctypes.c_int32),
+        ("reserved", ctypes.c_int32 * 3),
     ]
 
 
@@ -101,6 +109,10 @@ def library():
     missing = [name for name in EXPORTED if not hasattr(lib, name)]
     if missing:
         raise NativeLibraryError(f"{LIB_PATH} lacks exported symbols {missing}")
+    lib.fgw_mha_abi_version.restype = ctypes.c_int
+    if lib.fgw_mha_abi_version() != ABI_VERSION:
+        raise NativeLibraryError(f"{LIB_PATH} has ABI version {lib.fgw_mha_abi_version()}, this binding expects "
+                                 f"{ABI_VERSION}: rebuild with `python -m fgw_b200.build`")
     p = ctypes.POINTER(Params)
     vp = ctypes.c_void_p
     lib.fgw_mha_abi_version.argtypes = []

@@ -3,6 +3,7 @@
 // cube_general.py:186-188, 284-288): one launch when there is one split, partial then merge
 // otherwise, all on the caller's stream. A small planning launch precedes them and replaces the
 // reference's host copy of the cache lengths (v7.py:548).
+#include <algorithm>
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
@@ -28,6 +29,53 @@ EncodeTiledFn encode_tiled() {
   return fn;
 }
 
+// FGW_MHA_TENSOR_SINGLE_TILE=1 selects the one-query-tile tensor kernel for every head dimension
+// (the two-tile kernel is the default for head_dim <= 128); read once per process.
+static bool single_tile_requested() {
+  static const bool value = [] {
+    const char* v = std::getenv("FGW_MHA_TENSOR_SINGLE_TILE");
+    return v != nullptr && v[0] == '1';
+  }();
+  return value;
+}
+
+long long pair_items(const fgw_mha_params& p) {
+  return static_cast<long long>(p.batch) * p.heads * p.num_splits * ((p.q_len + kPairRows - 1) / kPairRows);
+}
+
+// AUTO takes the contiguous schedule only when whole items would leave more than a third of the programs
+// idle in their single wave (items < 2/3 of the programs): measured on config 2 (256 items, 148 programs,
+// two waves) the strided schedule is faster, since cutting items adds segment starts and piece merges.
+bool use_stream_schedule(const fgw_mha_params& p) {
+  if (p.schedule == FGW_SCHEDULE_STRIDED) return false;
+  const bool applies = resolve_path(p) == FGW_PATH_TENSOR && p.head_dim <= 128 && p.num_splits == 1 &&
+                       !single_tile_requested() && pair_items(p) <= kStreamMaxItems;
+  if (!applies) return false;
+  return p.schedule == FGW_SCHEDULE_CONTIGUOUS || 3 * pair_items(p) < 2ll * kStreamMaxPrograms;
+}
+
+namespace {
+// Byte sizes of the contiguous-schedule regions, in workspace order.
+struct StreamSizes {
+  size_t prog_item, prog_off, prog_u, prefix, counters, slot_lse, slot_o;
+  size_t total() const { return prog_item + prog_off + prog_u + prefix + counters + slot_lse + slot_o; }
+};
+
+StreamSizes stream_sizes(const fgw_mha_params& p) {
+  const size_t programs = kStreamMaxPrograms;
+  const size_t items = static_cast<size_t>(pair_items(p));
+  StreamSizes z;
+  z.prog_item = align256(programs * sizeof(int32_t));
+  z.prog_off = align256(programs * sizeof(int32_t));
+  z.prog_u = align256((programs + 1) * sizeof(long long));
+  z.prefix = align256((items + 1) * sizeof(long long));
+  z.counters = align256(items * sizeof(int32_t));
+  z.slot_lse = align256(2 * programs * kPairRows * sizeof(float));
+  z.slot_o = align256(2 * programs * kPairRows * static_cast<size_t>(p.head_dim) * sizeof(float));
+  return z;
+}
+}  // namespace
+
 size_t workspace_bytes(const fgw_mha_params& p, int /*path*/) {
   size_t bytes = sizeof(WorkspaceHeader);
   bytes += align256(sizeof(int32_t) * p.batch);  // lens
@@ -37,6 +85,7 @@ size_t workspace_bytes(const fgw_mha_params& p, int /*path*/) {
     bytes += align256(rows * p.num_splits * sizeof(float));
     bytes += align256(rows * p.num_splits * p.head_dim * sizeof(float));
   }
+  if (use_stream_schedule(p)) bytes += stream_sizes(p).total();
   return bytes;
 }
 
@@ -51,8 +100,30 @@ void carve_workspace(LaunchDesc& d, void* workspace, int /*path*/) {
   base += align256(sizeof(int32_t) * p.batch);
   const size_t rows = static_cast<size_t>(p.batch) * p.q_len * p.heads;
   d.part_lse = reinterpret_cast<float*>(base);
-  base += align256(rows * p.num_splits * sizeof(float));
-  d.part_o = reinterpret_cast<float*>(base);
+  d.part_o = nullptr;
+  if (p.num_splits > 1) {
+    base += align256(rows * p.num_splits * sizeof(float));
+    d.part_o = reinterpret_cast<float*>(base);
+    base += align256(rows * p.num_splits * p.head_dim * sizeof(float));
+  }
+  d.contiguous = use_stream_schedule(p);
+  if (d.contiguous) {
+    const StreamSizes z = stream_sizes(p);
+    d.items = static_cast<int>(pair_items(p));
+    d.prog_item = reinterpret_cast<int32_t*>(base);
+    base += z.prog_item;
+    d.prog_off = reinterpret_cast<int32_t*>(base);
+    base += z.prog_off;
+    d.prog_u = reinterpret_cast<long long*>(base);
+    base += z.prog_u;
+    d.prefix = reinterpret_cast<long long*>(base);
+    base += z.prefix;
+    d.counters = reinterpret_cast<int32_t*>(base);
+    base += z.counters;
+    d.slot_lse = reinterpret_cast<float*>(base);
+    base += z.slot_lse;
+    d.slot_o = reinterpret_cast<float*>(base);
+  }
 }
 
 int resolve_path(const fgw_mha_params& p) {
@@ -77,7 +148,8 @@ static int validate(const fgw_mha_params* p) {
   if (p->num_splits < 1 || p->num_splits > 1024) return FGW_ERR_INVALID_ARGUMENT;
   if (p->grid_cap < 0 || p->wait_budget_ms < 0) return FGW_ERR_INVALID_ARGUMENT;
   if (p->path < FGW_PATH_AUTO || p->path > FGW_PATH_TENSOR) return FGW_ERR_INVALID_ARGUMENT;
-  for (int i = 0; i < 4; ++i) {
+  if (p->schedule < FGW_SCHEDULE_AUTO || p->schedule > FGW_SCHEDULE_CONTIGUOUS) return FGW_ERR_INVALID_ARGUMENT;
+  for (int i = 0; i < 3; ++i) {
     if (p->reserved[i] != 0) return FGW_ERR_INVALID_ARGUMENT;
   }
   if (!p->q || !p->k_cache || !p->v_cache || !p->block_table || !p->cache_seqlens || !p->out) {
@@ -105,16 +177,6 @@ static int device_sm_count_cached(int device, int* sms) {
   return FGW_OK;
 }
 
-// FGW_MHA_TENSOR_SINGLE_TILE=1 selects the one-query-tile tensor kernel for every head dimension
-// (the two-tile kernel is the default for head_dim <= 128); read once per process.
-static bool single_tile_requested() {
-  static const bool value = [] {
-    const char* v = std::getenv("FGW_MHA_TENSOR_SINGLE_TILE");
-    return v != nullptr && v[0] == '1';
-  }();
-  return value;
-}
-
 static int prepare(const fgw_mha_params* params, void* workspace, size_t workspace_bytes_given, void* stream,
                    LaunchDesc& d) {
   int st = validate(params);
@@ -134,6 +196,10 @@ static int prepare(const fgw_mha_params* params, void* workspace, size_t workspa
   d.budget_ns = static_cast<uint64_t>(budget_ms) * 1000000ull;
   d.stream = static_cast<cudaStream_t>(stream);
   d.single_tile = single_tile_requested();
+  if (d.contiguous) {
+    const int cap = d.p.grid_cap > 0 ? d.p.grid_cap : d.sm_count;
+    d.programs = std::min(std::min(cap, d.sm_count), kStreamMaxPrograms);
+  }
   return FGW_OK;
 }
 

@@ -5,6 +5,8 @@
 //   round-robin start with the longest requests (longest-processing-time-first). This is the
 //   length-aware part of the reference's persistent scheduler (v7.py:112-113, 260-270), moved
 //   onto the device so no length ever has to cross to the host.
+//   With the contiguous schedule it also lays the two-tile kernel's work items end to end and cuts
+//   them into one equal range of KV tiles per program (StreamPlanArgs below).
 // merge_kernel: LSE-weighted merge of split-KV partials, one warp per output row; replaces the
 //   reference merge prim_funcs (v7.py:317-371, cube_general.py:224-279). Partials carry a base-2
 //   LSE; the empty-split sentinel and validity threshold keep the reference's -1e30 / -1e29.
@@ -15,10 +17,40 @@ namespace fgw {
 
 constexpr int kPlanSortMax = 8192;
 
+// Contiguous schedule, planned on the device from the clamped lengths: the work items of the two-tile
+// kernel in its item order, each counting max(KV tiles, 1) units; program p gets units
+// [p * (total / G) + min(p, total % G), ...) as in the reference's balanced plan (static_schedule.py:64-66).
+struct StreamPlanArgs {
+  int enabled, items, programs, heads, sq, causal, qpairs;
+  int32_t* prog_item;
+  int32_t* prog_off;
+  long long* prog_u;
+  long long* prefix;
+  int32_t* counters;
+};
+
+// Units of work item `item` (KV tiles seen by its last query row; at least 1): the two-tile kernel's
+// item decomposition with one split (pair_item in fgw_fmha2_sm100.cu).
+__device__ __forceinline__ long long stream_item_units(const StreamPlanArgs& s, const int32_t* lens,
+                                                       const int32_t* order, int item) {
+  const int p_rev = item % s.qpairs;
+  const int b = order[(item / s.qpairs) / s.heads];
+  const int q0 = (s.qpairs - 1 - p_rev) * 256;
+  const int last = min(q0 + 256, s.sq) - 1;
+  const int len = lens[b];
+  const int visible = s.causal ? max(len - s.sq + last + 1, 0) : len;
+  return max((visible + 127) / 128, 1);
+}
+
+__device__ __forceinline__ long long stream_program_start(long long total, int programs, int p) {
+  return static_cast<long long>(p) * (total / programs) + min(static_cast<long long>(p), total % programs);
+}
+
 __global__ void __launch_bounds__(1024) plan_kernel(const int32_t* __restrict__ lengths, int32_t* __restrict__ lens,
                                                    int32_t* __restrict__ order, WorkspaceHeader* ws, int batch,
-                                                   int capacity) {
+                                                   int capacity, StreamPlanArgs sp) {
   extern __shared__ unsigned long long keys[];
+  __shared__ long long chunk_sum[1024];
   if (threadIdx.x == 0) {
     ws->error = 0;
     ws->error_site = 0;
@@ -28,36 +60,88 @@ __global__ void __launch_bounds__(1024) plan_kernel(const int32_t* __restrict__ 
   }
   if (batch > kPlanSortMax) {
     for (int i = threadIdx.x; i < batch; i += blockDim.x) order[i] = i;
-    return;
-  }
-  int n = 1;
-  while (n < batch) n <<= 1;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    if (i < batch) {
-      const unsigned len = static_cast<unsigned>(min(max(lengths[i], 0), capacity));
-      keys[i] = (static_cast<unsigned long long>(0x7fffffffu - len) << 32) | static_cast<unsigned>(i);
-    } else {
-      keys[i] = ~0ull;
+  } else {
+    int n = 1;
+    while (n < batch) n <<= 1;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      if (i < batch) {
+        const unsigned len = static_cast<unsigned>(min(max(lengths[i], 0), capacity));
+        keys[i] = (static_cast<unsigned long long>(0x7fffffffu - len) << 32) | static_cast<unsigned>(i);
+      } else {
+        keys[i] = ~0ull;
+      }
     }
-  }
-  __syncthreads();
-  for (int k = 2; k <= n; k <<= 1) {
-    for (int j = k >> 1; j > 0; j >>= 1) {
-      for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        const int ixj = i ^ j;
-        if (ixj > i) {
-          const bool ascending = (i & k) == 0;
-          const unsigned long long x = keys[i], y = keys[ixj];
-          if ((x > y) == ascending) {
-            keys[i] = y;
-            keys[ixj] = x;
+    __syncthreads();
+    for (int k = 2; k <= n; k <<= 1) {
+      for (int j = k >> 1; j > 0; j >>= 1) {
+        for (int i = threadIdx.x; i < n; i += blockDim.x) {
+          const int ixj = i ^ j;
+          if (ixj > i) {
+            const bool ascending = (i & k) == 0;
+            const unsigned long long x = keys[i], y = keys[ixj];
+            if ((x > y) == ascending) {
+              keys[i] = y;
+              keys[ixj] = x;
+            }
           }
         }
+        __syncthreads();
       }
-      __syncthreads();
+    }
+    for (int i = threadIdx.x; i < batch; i += blockDim.x) order[i] = static_cast<int32_t>(keys[i] & 0xffffffffu);
+  }
+  if (!sp.enabled) return;
+  __syncthreads();  // lens and order are read below by other threads of this block
+  // exclusive prefix of item units: each thread sums a contiguous chunk, the chunk sums are scanned
+  const int per = (sp.items + blockDim.x - 1) / blockDim.x;
+  const int lo = min(sp.items, static_cast<int>(threadIdx.x) * per);
+  const int hi = min(sp.items, lo + per);
+  long long local = 0;
+  for (int i = lo; i < hi; ++i) {
+    local += stream_item_units(sp, lens, order, i);
+    sp.counters[i] = 0;
+  }
+  chunk_sum[threadIdx.x] = local;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    long long run = 0;
+    for (int t = 0; t < static_cast<int>(blockDim.x); ++t) {
+      const long long v = chunk_sum[t];
+      chunk_sum[t] = run;
+      run += v;
+    }
+    sp.prefix[sp.items] = run;
+  }
+  __syncthreads();
+  long long run = chunk_sum[threadIdx.x];
+  for (int i = lo; i < hi; ++i) {
+    sp.prefix[i] = run;
+    run += stream_item_units(sp, lens, order, i);
+  }
+  __syncthreads();
+  // program starts: the item holding unit U_p (the last item whose first unit is <= U_p)
+  const long long total = sp.prefix[sp.items];
+  for (int p = threadIdx.x; p <= sp.programs; p += blockDim.x) {
+    const long long u = stream_program_start(total, sp.programs, p);
+    sp.prog_u[p] = u;
+    if (p == sp.programs) continue;
+    int a = 0, b = sp.items;  // prefix[a] <= u < prefix[b] (b == items when u == total)
+    while (b - a > 1) {
+      const int mid = (a + b) / 2;
+      if (sp.prefix[mid] <= u) {
+        a = mid;
+      } else {
+        b = mid;
+      }
+    }
+    if (u >= total) {
+      sp.prog_item[p] = sp.items;
+      sp.prog_off[p] = 0;
+    } else {
+      sp.prog_item[p] = a;
+      sp.prog_off[p] = static_cast<int32_t>(u - sp.prefix[a]);
     }
   }
-  for (int i = threadIdx.x; i < batch; i += blockDim.x) order[i] = static_cast<int32_t>(keys[i] & 0xffffffffu);
 }
 
 cudaError_t launch_plan(const LaunchDesc& d) {
@@ -65,12 +149,27 @@ cudaError_t launch_plan(const LaunchDesc& d) {
   int n = 1;
   while (n < batch) n <<= 1;
   const size_t smem = batch <= kPlanSortMax ? n * sizeof(unsigned long long) : 0;
-  if (smem > 48 * 1024) {
+  if (smem > 32 * 1024) {
     cudaError_t err = cudaFuncSetAttribute(plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (err != cudaSuccess) return err;
   }
+  StreamPlanArgs sp{};
+  if (d.contiguous) {
+    sp.enabled = 1;
+    sp.items = d.items;
+    sp.programs = d.programs;
+    sp.heads = d.p.heads;
+    sp.sq = d.p.q_len;
+    sp.causal = d.p.causal;
+    sp.qpairs = (d.p.q_len + kPairRows - 1) / kPairRows;
+    sp.prog_item = d.prog_item;
+    sp.prog_off = d.prog_off;
+    sp.prog_u = d.prog_u;
+    sp.prefix = d.prefix;
+    sp.counters = d.counters;
+  }
   plan_kernel<<<1, 1024, smem, d.stream>>>(d.p.cache_seqlens, d.lens, d.order, d.header, batch,
-                                          d.p.table_width * d.p.page_size);
+                                          d.p.table_width * d.p.page_size, sp);
   return cudaGetLastError();
 }
 

@@ -137,6 +137,13 @@ __device__ __forceinline__ bool mbar_wait_all(uint64_t* b0, uint32_t p0, uint64_
   }
 }
 
+// Acquire load of a global word at GPU scope (a flag or counter written by other CTAs).
+__device__ __forceinline__ int ld_acquire_gpu(const int32_t* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
 // Named barrier over a subset of warps (id 0 is __syncthreads).
 __device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");

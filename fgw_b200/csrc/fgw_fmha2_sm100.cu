@@ -31,6 +31,15 @@ struct Fmha2Args {
   WorkspaceHeader* ws;
   int batch, sq, heads, dim, width, page, splits, causal, box_rows, write_partials, qpairs;
   long long items;
+  // contiguous schedule (see fgw_schedule): per-program start item / unit offset / first unit, the
+  // per-item arrival counters and the two partial slots of every program
+  int contiguous, programs;
+  const int32_t* prog_item;
+  const int32_t* prog_off;
+  const long long* prog_u;
+  int32_t* counters;
+  float* slot_lse;
+  float* slot_o;
   float scale_log2;
   uint64_t budget_ns;
 };
@@ -113,6 +122,91 @@ __device__ __forceinline__ void exp2_pack_half(const uint32_t* sr, float2 scale2
   }
 }
 
+// One run of KV tiles of one work item processed by this CTA. With the strided schedule a segment is a
+// whole item; with the contiguous schedule it may be a piece of an item cut between programs.
+struct Segment {
+  PairItem c;        // n_begin / n / n_tile[] restricted to the segment's KV tiles
+  int item;
+  bool piece;        // the item's other tiles belong to other programs
+  long long item_u;  // first unit of the item (contiguous schedule)
+  long long u0;      // first unit of this segment (contiguous schedule)
+  int units;         // units of the whole item (contiguous schedule)
+};
+
+struct SegmentCursor {
+  long long item;
+  int off;
+  long long u, u_end;
+};
+
+__device__ __forceinline__ void cursor_init(const Fmha2Args& a, SegmentCursor& k) {
+  if (a.contiguous) {
+    k.item = a.prog_item[blockIdx.x];
+    k.off = a.prog_off[blockIdx.x];
+    k.u = a.prog_u[blockIdx.x];
+    k.u_end = a.prog_u[blockIdx.x + 1];
+  } else {
+    k.item = blockIdx.x;
+    k.off = 0;
+    k.u = k.u_end = 0;
+  }
+}
+
+// Every role of the CTA walks the same segments in the same order.
+__device__ __forceinline__ bool next_segment(const Fmha2Args& a, SegmentCursor& k, Segment& sg) {
+  if (!a.contiguous) {
+    if (k.item >= a.items) return false;
+    sg.item = static_cast<int>(k.item);
+    pair_item(a, k.item, sg.c);
+    sg.piece = false;
+    sg.item_u = sg.u0 = 0;
+    sg.units = 0;
+    k.item += gridDim.x;
+    return true;
+  }
+  if (k.u >= k.u_end) return false;
+  sg.item = static_cast<int>(k.item);
+  pair_item(a, k.item, sg.c);  // one split: the whole item
+  const int tiles = sg.c.n;
+  sg.units = max(tiles, 1);    // an item without keys still costs one unit (its rows are written as zeros)
+  const int first = k.off;
+  const int count = static_cast<int>(min(static_cast<long long>(sg.units - first), k.u_end - k.u));
+  sg.u0 = k.u;
+  sg.item_u = k.u - first;
+  sg.piece = count < sg.units;
+  const int tiles_a = sg.c.n_tile[0];
+  const bool has_b = sg.c.n_tile[1] > 0;
+  const int real = max(0, min(first + count, tiles) - first);
+  sg.c.n_begin = first;
+  sg.c.n = real;
+  sg.c.n_tile[0] = max(0, min(first + count, tiles_a) - first);
+  sg.c.n_tile[1] = has_b ? real : 0;
+  k.u += count;
+  k.off += count;
+  if (k.off >= sg.units) {
+    ++k.item;
+    k.off = 0;
+  }
+  return true;
+}
+
+// Contiguous schedule: program p owns units [start(p), start(p + 1)), start(p) = p (T / G) + min(p, T % G).
+__device__ __forceinline__ long long program_start(long long total, int programs, int p) {
+  return static_cast<long long>(p) * (total / programs) + min(static_cast<long long>(p), total % programs);
+}
+
+__device__ __forceinline__ int program_of(long long total, int programs, long long u) {
+  const long long b = total / programs, r = total % programs;
+  if (u < r * (b + 1)) return static_cast<int>(u / (b + 1));
+  return static_cast<int>(r + (u - r * (b + 1)) / b);
+}
+
+// Partial slot of item piece held by program q: slot 2q for the program's first segment, 2q + 1 for its
+// last (a program holds at most two pieces: one it starts with, one it ends with).
+__device__ __forceinline__ int piece_slot(long long total, int programs, int q, int q_first, long long item_u) {
+  return 2 * q + ((q == q_first && item_u != program_start(total, programs, q)) ? 1 : 0);
+}
+
 template <typename T, int NB>
 __global__ void __launch_bounds__(384, 1)
     fmha2_sm100_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
@@ -169,7 +263,6 @@ __global__ void __launch_bounds__(384, 1)
   __syncthreads();
   tc_fence_after_sync();
   const uint32_t tmem = *tmem_slot;
-  const int grid = gridDim.x;
   const int D = a.dim;
 
   if (warp < 4) setmaxnreg_dec<S::kRegsControl>();  // warpgroup 0: TMA, MMA and two idle warps
@@ -187,9 +280,11 @@ __global__ void __launch_bounds__(384, 1)
         ok = false;
         record_error(a.ws, FGW_ERR_DEVICE_TIMEOUT, site);
       };
-      for (long long item = blockIdx.x; item < a.items; item += grid) {
-        PairItem c;
-        pair_item(a, item, c);
+      SegmentCursor cur;
+      cursor_init(a, cur);
+      Segment sg;
+      while (next_segment(a, cur, sg)) {
+        const PairItem& c = sg.c;
         if (c.n <= 0) continue;
         if (ok && !mbar_wait(q_empty, (qc & 1) ^ 1, a.budget_ns)) fail(40);
         if (ok) {
@@ -288,9 +383,11 @@ __global__ void __launch_bounds__(384, 1)
                         (!first || kk > 0) ? 1u : 0u);
         }
       };
-      for (long long item = blockIdx.x; item < a.items; item += grid) {
-        PairItem c;
-        pair_item(a, item, c);
+      SegmentCursor cur;
+      cursor_init(a, cur);
+      Segment sg;
+      while (next_segment(a, cur, sg)) {
+        const PairItem& c = sg.c;
         if (c.n <= 0) continue;
         // prologue: S_A(0), S_B(0) once Q and K(0) are in
         int kst = kc % NS;
@@ -372,9 +469,12 @@ __global__ void __launch_bounds__(384, 1)
       }
       return ok;
     };
-    for (long long item = blockIdx.x; item < a.items; item += grid) {
-      PairItem c;
-      pair_item(a, item, c);
+    volatile int* merge_flag = reinterpret_cast<volatile int*>(smem + S::kTmemSlot + 4);
+    SegmentCursor cur;
+    cursor_init(a, cur);
+    Segment sg;
+    while (next_segment(a, cur, sg)) {
+      const PairItem& c = sg.c;
       const int q = c.q0 + 128 * t + row;
       const bool row_valid = q < a.sq;
       const int vis = row_valid ? visible_upto(q, c.len, a.sq, a.causal) : 0;
@@ -495,8 +595,9 @@ __global__ void __launch_bounds__(384, 1)
         if (ok) tc_fence_after_sync();
       }
       const long long row_id = row_valid ? ((long long)c.b * a.sq + q) * a.heads + c.h : 0;
-      for (int cb = 0; cb < D / 16; ++cb) {
-        float o[16];
+      const float own_lse = (n_t > 0 && l > 0.f) ? m + fast_log2(l) : kEmptyLse;
+      // this row's O block cb (16 columns), normalised, from TMEM
+      auto load_o = [&](int cb, float (&o)[16]) {
         if (n_t > 0 && ok) {
           uint32_t r[16];
           tmem_ld16(o_addr + cb * 16, r);
@@ -507,21 +608,113 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll
           for (int i = 0; i < 16; ++i) o[i] = 0.f;
         }
-        if (!row_valid) continue;
-        if (a.write_partials) {
-          float4* dst = reinterpret_cast<float4*>(a.part_o + (row_id * a.splits + c.s) * D + cb * 16);
+      };
+      auto store_row = [&](int cb, const float (&o)[16], float scale) {
+        uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<T*>(a.out) + row_id * D + cb * 16);
+        dst[0] = make_uint4(Tr::pack2(o[0] * scale, o[1] * scale), Tr::pack2(o[2] * scale, o[3] * scale),
+                            Tr::pack2(o[4] * scale, o[5] * scale), Tr::pack2(o[6] * scale, o[7] * scale));
+        dst[1] = make_uint4(Tr::pack2(o[8] * scale, o[9] * scale), Tr::pack2(o[10] * scale, o[11] * scale),
+                            Tr::pack2(o[12] * scale, o[13] * scale), Tr::pack2(o[14] * scale, o[15] * scale));
+      };
+      if (!sg.piece) {
+        for (int cb = 0; cb < D / 16; ++cb) {
+          float o[16];
+          load_o(cb, o);  // warp-collective: every lane, valid row or not
+          if (row_valid && a.write_partials) {
+            float4* dst = reinterpret_cast<float4*>(a.part_o + (row_id * a.splits + c.s) * D + cb * 16);
 #pragma unroll
-          for (int i = 0; i < 4; ++i) dst[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
-        } else {
-          uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<T*>(a.out) + row_id * D + cb * 16);
-          dst[0] = make_uint4(Tr::pack2(o[0], o[1]), Tr::pack2(o[2], o[3]), Tr::pack2(o[4], o[5]),
-                              Tr::pack2(o[6], o[7]));
-          dst[1] = make_uint4(Tr::pack2(o[8], o[9]), Tr::pack2(o[10], o[11]), Tr::pack2(o[12], o[13]),
-                              Tr::pack2(o[14], o[15]));
+            for (int i = 0; i < 4; ++i) dst[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+          } else if (row_valid) {
+            store_row(cb, o, 1.f);
+          }
         }
-      }
-      if (row_valid && a.write_partials) {
-        a.part_lse[row_id * a.splits + c.s] = (n_t > 0 && l > 0.f) ? m + fast_log2(l) : kEmptyLse;
+        if (row_valid && a.write_partials) a.part_lse[row_id * a.splits + c.s] = own_lse;
+      } else {
+        // A piece of an item cut between programs. Pieces count themselves in (arrival counter per item)
+        // only after writing their partial to this program's slot (2 p for the piece a program starts with,
+        // 2 p + 1 for the one it ends with). The piece that finds every other piece already counted merges
+        // them with its own O straight from TMEM and writes nothing else; if two pieces race past that check,
+        // both write and the one whose count completes the set merges. No CTA ever waits for another.
+        const long long total = a.prog_u[a.programs];
+        const int q_first = program_of(total, a.programs, sg.item_u);
+        const int pieces = program_of(total, a.programs, sg.item_u + sg.units - 1) - q_first + 1;
+        const int first_extra = sg.item_u != program_start(total, a.programs, q_first) ? 1 : 0;
+        const int own = blockIdx.x - q_first;
+        // slot row of piece k, relative to piece 0's (piece k >= 1 sits 2k - first_extra slots later)
+        auto piece_row = [&](int k) -> long long {
+          return (2ll * q_first + first_extra + (k == 0 ? 0 : 2 * k - first_extra)) * kPairRows + 128 * t + row;
+        };
+        if (warp == 4 && lane == 0) *merge_flag = ld_acquire_gpu(&a.counters[sg.item]) == pieces - 1 ? 1 : 0;
+        named_barrier_sync(1, 256);
+        int merge = *merge_flag;
+        named_barrier_sync(1, 256);  // read by all before the next write
+        if (!merge) {
+          const long long my_row = piece_row(own);
+          for (int cb = 0; cb < D / 16; ++cb) {
+            float o[16];
+            load_o(cb, o);  // warp-collective: every lane, valid row or not
+            if (row_valid) {
+              float4* dst = reinterpret_cast<float4*>(a.slot_o + my_row * D + cb * 16);
+#pragma unroll
+              for (int i = 0; i < 4; ++i) dst[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+            }
+          }
+          if (row_valid) a.slot_lse[my_row] = own_lse;
+          named_barrier_sync(1, 256);  // both warpgroups have written their rows
+          if (warp == 4 && lane == 0) {
+            __threadfence();
+            *merge_flag = atomicAdd(&a.counters[sg.item], 1) + 1 == pieces ? 1 : 0;
+          }
+          named_barrier_sync(1, 256);
+          merge = *merge_flag;
+          named_barrier_sync(1, 256);
+        }
+        if (merge) {
+          __threadfence();
+          if (warp == 4 && lane == 0) a.counters[sg.item] = 0;  // ready for the next launch
+          // base-2 LSE merge (the split merge's arithmetic, merge_kernel in fgw_aux.cu); own piece from TMEM.
+          // Every lane runs the TMEM loads (warp-collective); only valid rows touch global memory.
+          float peak = own_lse;
+          float wsum = 0.f;
+          if (row_valid) {
+            for (int k = 0; k < pieces; ++k) {
+              if (k != own) peak = fmaxf(peak, __ldcg(&a.slot_lse[piece_row(k)]));
+            }
+            for (int k = 0; k < pieces; ++k) {
+              if (k == own) continue;
+              const float lse = __ldcg(&a.slot_lse[piece_row(k)]);
+              if (lse > kValidLse) wsum += fast_exp2(lse - peak);
+            }
+          }
+          const float w_own = own_lse > kValidLse ? fast_exp2(own_lse - peak) : 0.f;
+          wsum += w_own;
+          const float scale = wsum > 0.f ? 1.f / wsum : 0.f;
+          for (int cb = 0; cb < D / 16; ++cb) {
+            float acc[16];
+            load_o(cb, acc);  // warp-collective: every lane, valid row or not
+            if (row_valid) {
+#pragma unroll
+              for (int i = 0; i < 16; ++i) acc[i] *= w_own;
+              for (int k = 0; k < pieces; ++k) {
+                if (k == own) continue;
+                const long long pr = piece_row(k);
+                const float lse = __ldcg(&a.slot_lse[pr]);
+                if (!(lse > kValidLse)) continue;
+                const float w = fast_exp2(lse - peak);
+                const float4* src = reinterpret_cast<const float4*>(a.slot_o + pr * D + cb * 16);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                  const float4 v = __ldcg(src + i);
+                  acc[4 * i] += w * v.x;
+                  acc[4 * i + 1] += w * v.y;
+                  acc[4 * i + 2] += w * v.z;
+                  acc[4 * i + 3] += w * v.w;
+                }
+              }
+              store_row(cb, acc, scale);
+            }
+          }
+        }
       }
       if (n_t > 0) {
         tc_fence_before_sync();
@@ -554,7 +747,9 @@ static cudaError_t launch_fmha2_t(const LaunchDesc& d, const Fmha2Args& args, co
   err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kBytes);
   if (err != cudaSuccess) return err;
   const long long cap = d.p.grid_cap > 0 ? d.p.grid_cap : d.sm_count;
-  const long long grid = std::min<long long>(args.items, std::min<long long>(cap, d.sm_count));
+  // contiguous schedule: one CTA per program of the plan; strided: persistent CTAs over the items
+  const long long grid = args.contiguous ? args.programs
+                                         : std::min<long long>(args.items, std::min<long long>(cap, d.sm_count));
   if (grid <= 0) return cudaSuccess;
   kernel<<<(unsigned)grid, S::kThreads, S::kBytes, d.stream>>>(qmap, kmap, vmap, args);
   return cudaGetLastError();
@@ -585,6 +780,14 @@ cudaError_t launch_tensor_pairs(const LaunchDesc& d, bool write_partials, const 
   args.items = (long long)p.batch * p.heads * p.num_splits * args.qpairs;
   args.scale_log2 = (1.0f / sqrtf((float)p.head_dim)) * kLog2e;
   args.budget_ns = d.budget_ns;
+  args.contiguous = d.contiguous ? 1 : 0;
+  args.programs = d.contiguous ? d.programs : 0;
+  args.prog_item = d.prog_item;
+  args.prog_off = d.prog_off;
+  args.prog_u = d.prog_u;
+  args.counters = d.counters;
+  args.slot_lse = d.slot_lse;
+  args.slot_o = d.slot_o;
   const bool bf16 = p.dtype == FGW_DTYPE_BFLOAT16;
   if (p.head_dim <= 64) {
     return bf16 ? launch_fmha2_t<__nv_bfloat16, 1>(d, args, qmap, kmap, vmap)

@@ -11,6 +11,13 @@ namespace fgw {
 
 struct WorkspaceHeader;
 
+// Contiguous schedule (fgw_schedule CONTIGUOUS): at most this many programs (persistent CTAs), and at
+// most this many work items to lay end to end (the plan launch scans them in one CTA).
+constexpr int kStreamMaxPrograms = 148;
+constexpr int kStreamMaxItems = 65536;
+// rows of one work item of the two-tile kernel (two 128-row query tiles)
+constexpr int kPairRows = 256;
+
 // Resolved launch description shared by every kernel family.
 struct LaunchDesc {
   fgw_mha_params p;
@@ -20,13 +27,31 @@ struct LaunchDesc {
   int32_t* order;     // [batch] batch rows by descending cache length
   float* part_o;      // [batch*q_len*heads, splits, head_dim] FP32 normalised partial outputs
   float* part_lse;    // [batch*q_len*heads, splits] base-2 LSE per partial
+  // contiguous schedule (contiguous == true): per-program start item / offset (in KV tiles) / first unit,
+  // prog_u[programs] = total units; per-item arrival counters; two partial slots per program
+  bool contiguous;
+  int programs;
+  int items;
+  int32_t* prog_item;  // [programs]
+  int32_t* prog_off;   // [programs]
+  long long* prog_u;   // [programs + 1]
+  long long* prefix;   // [items + 1] plan scratch: first unit of every item
+  int32_t* counters;   // [items]
+  float* slot_lse;     // [2 * programs, kPairRows] base-2 LSE of each piece row
+  float* slot_o;       // [2 * programs, kPairRows, head_dim] FP32 normalised piece outputs
   uint64_t budget_ns;
   int sm_count;
   bool single_tile;   // force the one-query-tile tensor kernel (FGW_MHA_TENSOR_SINGLE_TILE set)
   cudaStream_t stream;
 };
 
-// Workspace layout: header | lens | order | part_lse | part_o, each 256-byte aligned.
+// Work items of the two-tile tensor kernel: batch x heads x splits x ceil(q_len / 256).
+long long pair_items(const fgw_mha_params& p);
+// Whether the main launch runs the contiguous schedule (the two-tile kernel with fused piece merge).
+bool use_stream_schedule(const fgw_mha_params& p);
+
+// Workspace layout: header | lens | order | part_lse | part_o | (contiguous schedule: prog_item | prog_off |
+// prog_u | prefix | counters | slot_lse | slot_o), each 256-byte aligned.
 size_t workspace_bytes(const fgw_mha_params& p, int path);
 void carve_workspace(LaunchDesc& d, void* workspace, int path);
 

@@ -43,9 +43,16 @@ int static_workspace_ptr(void** ptr) {
 
 extern "C" int fgw_mha_paged_fwd_static_ws(const fgw_mha_params* params, void* stream) {
   if (params == nullptr) return FGW_ERR_INVALID_ARGUMENT;
+  fgw_mha_params p = *params;
   size_t needed = 0;
-  int st = fgw_mha_workspace_size(params, &needed);
+  int st = fgw_mha_workspace_size(&p, &needed);
   if (st != FGW_OK) return st;
+  if (needed > static_cast<size_t>(FGW_MHA_STATIC_WORKSPACE_BYTES) && p.schedule == FGW_SCHEDULE_AUTO) {
+    // The contiguous schedule's partial slots do not fit: the strided schedule needs no slots.
+    p.schedule = FGW_SCHEDULE_STRIDED;
+    st = fgw_mha_workspace_size(&p, &needed);
+    if (st != FGW_OK) return st;
+  }
   if (needed > static_cast<size_t>(FGW_MHA_STATIC_WORKSPACE_BYTES)) return FGW_ERR_WORKSPACE_TOO_SMALL;
   void* ws = nullptr;
   st = static_workspace_ptr(&ws);
@@ -53,5 +60,5 @@ extern "C" int fgw_mha_paged_fwd_static_ws(const fgw_mha_params* params, void* s
   // The plan kernel that starts every forward clears the error word; every other byte of scratch the
   // kernels read (lengths, order, partials) is written earlier in the same call, so the previous
   // call's leftovers never reach an output.
-  return fgw_mha_paged_fwd(params, ws, FGW_MHA_STATIC_WORKSPACE_BYTES, stream);
+  return fgw_mha_paged_fwd(&p, ws, FGW_MHA_STATIC_WORKSPACE_BYTES, stream);
 }

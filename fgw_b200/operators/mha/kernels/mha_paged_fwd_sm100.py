@@ -20,6 +20,7 @@ callable; the CUDA kernels size their own TMA rings, so they do not change the s
 ``persistent_programs`` caps the persistent grid (default: the SM count; ``None`` uncapped).
 """
 import functools
+import os
 
 import torch
 
@@ -207,7 +208,16 @@ def build_kernel(batch, sq, heads, dim, pool_rows, width, page_size, causal, dty
     params.num_splits = splits
     params.grid_cap = grid_cap
     params.path = kernel_path
+    params.schedule = {None: _native.SCHEDULE_AUTO, "strided": _native.SCHEDULE_STRIDED,
+                       "contiguous": _native.SCHEDULE_CONTIGUOUS}[task_assignment]
     workspace_bytes = _native.workspace_size(params)
+    # The contiguous schedule applies to the two-tile tensor kernel with one split (fgw_schedule in
+    # include/fgw_mha.h); elsewhere the work items are dealt out strided in longest-request-first order.
+    pair_items = batch * heads * ((sq + 255) // 256)
+    contiguous = (kernel_path == _native.PATH_TENSOR and dim <= 128 and splits == 1
+                  and task_assignment != "strided" and pair_items <= 65536
+                  and os.environ.get("FGW_MHA_TENSOR_SINGLE_TILE") != "1"
+                  and (task_assignment == "contiguous" or 3 * pair_items < 2 * 148))
 
     def _bind(q, k, v, table, lengths, out):
         p = _native.Params.from_buffer_copy(params)
@@ -249,7 +259,10 @@ def build_kernel(batch, sq, heads, dim, pool_rows, width, page_size, causal, dty
 
     launch.block_q = block_q
     launch.compute_grid = compute_grid
-    launch.task_assignment = task_assignment or "lpt_round_robin"
+    launch.task_assignment = "contiguous" if contiguous else "strided"
+    if contiguous:
+        compute_grid = min(cores, 148) if grid_cap == 0 else min(grid_cap, cores, 148)
+        launch.compute_grid = compute_grid
     launch.compute_work = compute_work
     launch.persistent_programs = programs
     launch.requested_split_policy = requested_policy
@@ -303,7 +316,7 @@ def mha_paged_decode(q, k_cache, v_cache, block_table, cache_seqlens, page_size,
                      pipeline_stages=2, buffer_versions=2, q_resident=True, kv_versions=None,
                      schedule_mode="manual", num_splits=None, split_policy="auto",
                      persistent_programs=DEFAULT_PROGRAMS, cube_mode="stable", general_model_version=1,
-                     path="auto", cache_lengths=None, out=None):
+                     path="auto", cache_lengths=None, out=None, task_assignment=None):
     """Paged MHA forward: O[B,Sq,H,D] = softmax(Q K^T / sqrt(D)) V over each request's live pages.
 
     ``cache_lengths`` may pass the host copy of ``cache_seqlens`` when the caller already has it;
@@ -327,5 +340,5 @@ def mha_paged_decode(q, k_cache, v_cache, block_table, cache_seqlens, page_size,
                           persistent_programs=persistent_programs, cube_mode=cube_mode,
                           cache_lengths=model_lengths if selected_route != "cube_bf16_d128" or not full_kv_cache
                           else None,
-                          general_model_version=general_model_version, path=path)
+                          general_model_version=general_model_version, path=path, task_assignment=task_assignment)
     return kernel(q, k_cache, v_cache, block_table, cache_seqlens, out=out)

@@ -33,7 +33,7 @@
 extern "C" {
 #endif
 
-#define FGW_MHA_ABI_VERSION 1
+#define FGW_MHA_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define FGW_API __attribute__((visibility("default")))
@@ -59,6 +59,24 @@ typedef enum fgw_path {
   FGW_PATH_DECODE = 1, /* warp-level HBM-streaming kernel (any q_len; intended for q_len <= 8) */
   FGW_PATH_TENSOR = 2  /* tcgen05/TMEM kernel, 128-row query tiles */
 } fgw_path;
+
+/*
+ * How the main launch divides the work between its persistent CTAs (the reference's task_assignment,
+ * v7.py:112-113, 260-270, and its static host stream plan, operators/mha/static_schedule.py:48-80, 195-247).
+ *   STRIDED:    whole work items (request, head, split, query block), CTA i takes items i, i + grid, ...
+ *               in longest-request-first order.
+ *   CONTIGUOUS: the KV tiles of all work items, laid end to end, are cut into one contiguous range per CTA
+ *               of equal length (loads differ by at most one tile); an item cut between CTAs is computed in
+ *               pieces whose partial results the CTA finishing last merges in the same launch. Tensor path
+ *               with num_splits == 1 and head_dim <= 128 only.
+ *   AUTO:       CONTIGUOUS where it applies and there are fewer work items than 2/3 of 148 programs (whole
+ *               items would leave SMs idle), STRIDED otherwise.
+ */
+typedef enum fgw_schedule {
+  FGW_SCHEDULE_AUTO = 0,
+  FGW_SCHEDULE_STRIDED = 1,
+  FGW_SCHEDULE_CONTIGUOUS = 2
+} fgw_schedule;
 
 /*
  * Tensor contract (same as the reference, operators/mha/README.md:5):
@@ -92,7 +110,8 @@ typedef struct fgw_mha_params {
   int32_t grid_cap;    /* persistent CTAs for the main kernel; 0 = one per work item */
   int32_t path;        /* fgw_path */
   int32_t wait_budget_ms; /* device-side wait limit; 0 = default (2000 ms) */
-  int32_t reserved[4];    /* must be zero */
+  int32_t schedule;       /* fgw_schedule */
+  int32_t reserved[3];    /* must be zero */
 } fgw_mha_params;
 
 /* ABI version of the loaded library (FGW_MHA_ABI_VERSION it was built with). */

@@ -32,6 +32,38 @@ def test_kernel_path_matches_reference_golden(entry, path):
     _check(_run(inputs, path=path), expected, inputs)
 
 
+@pytest.mark.parametrize("entry", ENTRIES, ids=[e["key"] for e in ENTRIES])
+def test_tensor_strided_schedule_matches_reference_golden(entry):
+    # the default (contiguous, pieces merged in-kernel) is covered above; whole items, strided, here
+    case, seed, dtype, causal, pattern = entry_params(entry)
+    inputs = build_case(case, seed, dtype, causal, pattern)
+    expected = dtype_bits_to_f32(expected_bits(entry), dtype_name(dtype))
+    _check(_run(inputs, path="tensor", task_assignment="strided"), expected, inputs)
+
+
+@pytest.mark.parametrize("causal,programs", [(False, 1), (False, 3), (False, 7), (False, None), (True, 28),
+                                             (True, None)])
+def test_contiguous_schedule_pieces_merge_to_the_oracle(causal, programs):
+    # Few programs over many KV tiles: items are cut into pieces at arbitrary tile offsets, some items
+    # span many programs, and the last arriver of each merges them in the same launch. (The reference's
+    # general route, taken when causal, accepts only its default program caps.)
+    case = ("stream_pieces", 3, 600, 2, 128, 128, 20)  # B3 Sq600 (3 query pairs) H2 D128 page 128
+    from fixtures import make_inputs, poison_unread
+    q, k, v, table = make_inputs(case, 42, torch.bfloat16)
+    lengths = [2560, 1, 1333]
+    k, v = poison_unread(k, v, table, lengths, 128)
+    inputs = {"case": case, "seed": 42, "dtype": torch.bfloat16, "causal": causal, "pattern": "stream", "q": q,
+              "k": k, "v": v, "table": table, "lengths": torch.tensor(lengths, dtype=torch.int32)}
+    kwargs = dict(path="tensor", task_assignment="contiguous")
+    if programs is not None:
+        kwargs["persistent_programs"] = programs
+    out = _run(inputs, **kwargs)
+    _check(out, oracle_output(inputs), inputs)
+    # twice in a row: the arrival counters are reset for the next launch
+    out2 = _run(inputs, **kwargs)
+    assert torch.equal(out, out2)
+
+
 SPLIT_ENTRIES = [e for e in ENTRIES if e["seed"] == 7 and e["pattern"] == "mixed"]
 
 

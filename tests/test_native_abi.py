@@ -26,7 +26,7 @@ def test_library_loads_and_exports_every_declared_symbol():
     lib = _native.library()
     for name in declared_functions():
         assert hasattr(lib, name), name
-    assert _native.abi_version() == 1
+    assert _native.abi_version() == _native.ABI_VERSION == 2
 
 
 def test_status_strings():
@@ -36,9 +36,32 @@ def test_status_strings():
 
 
 def test_params_struct_layout_matches_header():
-    # int64 pool_rows after six pointers; 12 int32 fields + 4 reserved.
+    # int64 pool_rows after six pointers; 13 int32 fields (the last is schedule) + 3 reserved.
     assert _native.Params.pool_rows.offset == 6 * 8
+    assert _native.Params.schedule.offset == 6 * 8 + 8 + 12 * 4
     assert ctypes.sizeof(_native.Params) == 6 * 8 + 8 + 16 * 4
+
+
+def test_schedule_is_validated_and_sizes_the_workspace():
+    # contiguous schedule (tensor path, one split, head_dim <= 128) adds the plan arrays and partial slots
+    strided = _native.workspace_size(_params(q_len=4096, num_splits=1, path=_native.PATH_TENSOR,
+                                             schedule=_native.SCHEDULE_STRIDED))
+    contiguous = _native.workspace_size(_params(q_len=4096, num_splits=1, path=_native.PATH_TENSOR,
+                                                schedule=_native.SCHEDULE_CONTIGUOUS))
+    slots = 2 * 148 * 256 * (128 + 1) * 4
+    assert contiguous >= strided + slots
+    # AUTO: contiguous only with fewer than 2/3 x 148 work items (here 2 x 2 x 16 = 64)
+    assert _native.workspace_size(_params(q_len=4096, num_splits=1, path=_native.PATH_TENSOR)) == contiguous
+    many = dict(batch=8, heads=16, q_len=4096, num_splits=1, path=_native.PATH_TENSOR)  # 2048 items
+    assert (_native.workspace_size(_params(**many))
+            == _native.workspace_size(_params(schedule=_native.SCHEDULE_STRIDED, **many)))
+    with pytest.raises(_native.FgwError):
+        _native.check(_native.library().fgw_mha_paged_fwd(ctypes.byref(_params(schedule=3)), None, 0, None),
+                      "fgw_mha_paged_fwd")
+    # splits > 1 or the decode path keep the strided layout
+    assert (_native.workspace_size(_params(q_len=4096, num_splits=2, path=_native.PATH_TENSOR))
+            == _native.workspace_size(_params(q_len=4096, num_splits=2, path=_native.PATH_TENSOR,
+                                              schedule=_native.SCHEDULE_STRIDED)))
 
 
 def _params(**overrides):
