@@ -82,22 +82,32 @@ def barrier(world):
         dist.barrier()
 
 
-def max_over_ranks(value, world):
+def _reduce_over_ranks(value, world, op):
     if world == 1:
         return value
     import torch.distributed as dist
-    t = torch.tensor([value], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    device = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=op)
     return float(t.item())
+
+
+def max_over_ranks(value, world):
+    import torch.distributed as dist
+    return _reduce_over_ranks(value, world, dist.ReduceOp.MAX if world > 1 else None)
 
 
 def sum_over_ranks(value, world):
-    if world == 1:
-        return value
     import torch.distributed as dist
-    t = torch.tensor([value], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.SUM)
-    return float(t.item())
+    return _reduce_over_ranks(value, world, dist.ReduceOp.SUM if world > 1 else None)
+
+
+def head_shard(heads, rank, world):
+    """Decode is sharded by heads: rank r holds heads [r*H/N, (r+1)*H/N) of every page (H divisible by N)."""
+    if heads % world:
+        raise ValueError(f"{heads} heads do not split evenly over {world} ranks")
+    per = heads // world
+    return rank * per, per
 
 
 def measured_peaks():
@@ -146,7 +156,7 @@ def decode_inputs(seed, rank, world, device, batch):
         table[b, :n] = perm[start:start + n]
         start += n
     pool_rows = (total_pages + 8) * c["page"]
-    heads = c["heads"] // world
+    _, heads = head_shard(c["heads"], rank, world)
     gdev = torch.Generator(device=device).manual_seed(seed + 17 * rank)
     q = torch.randn(c["batch"], 1, heads, c["dim"], generator=gdev, device=device).to(torch.bfloat16)
     k = torch.empty(pool_rows, heads, c["dim"], dtype=torch.bfloat16, device=device)

@@ -45,6 +45,7 @@ EXPORTED = (
     "fgw_mha_merge",
     "fgw_mha_read_error",
     "fgw_mha_paged_fwd_static_ws",
+    "fgw_mha_selftest_wait",
 )
 
 STATIC_WORKSPACE_BYTES = 16 << 20  # FGW_MHA_STATIC_WORKSPACE_BYTES
@@ -131,6 +132,8 @@ def library():
         fn.restype = ctypes.c_int
     lib.fgw_mha_read_error.argtypes = [vp, vp, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int)]
     lib.fgw_mha_read_error.restype = ctypes.c_int
+    lib.fgw_mha_selftest_wait.argtypes = [vp, ctypes.c_size_t, ctypes.c_int, ctypes.c_int, vp]
+    lib.fgw_mha_selftest_wait.restype = ctypes.c_int
     lib.fgw_mha_paged_fwd_static_ws.argtypes = [p, vp]
     lib.fgw_mha_paged_fwd_static_ws.restype = ctypes.c_int
     _LIB = lib
@@ -202,6 +205,12 @@ def read_error(workspace_ptr, stream_ptr):
     check(library().fgw_mha_read_error(workspace_ptr, stream_ptr, ctypes.byref(status), ctypes.byref(site)),
           "fgw_mha_read_error")
     return status.value, site.value
+
+
+def selftest_wait(workspace_ptr, workspace_bytes, budget_ms, complete, stream_ptr):
+    """Bounded-wait self-test (see include/fgw_mha.h); read the outcome with read_error."""
+    check(library().fgw_mha_selftest_wait(workspace_ptr, workspace_bytes, budget_ms, 1 if complete else 0,
+                                          stream_ptr), "fgw_mha_selftest_wait")
 
 
 def paged_fwd_static_ws(params, stream_ptr):

@@ -302,6 +302,21 @@ int fgw_mha_merge(const fgw_mha_params* params, void* workspace, size_t workspac
   return launch_merge(d) == cudaSuccess ? FGW_OK : FGW_ERR_CUDA;
 }
 
+int fgw_mha_selftest_wait(void* workspace, size_t workspace_bytes, int budget_ms, int complete, void* stream) {
+  if (workspace == nullptr || (reinterpret_cast<uintptr_t>(workspace) & 255u) ||
+      workspace_bytes < sizeof(WorkspaceHeader) || budget_ms <= 0) {
+    return FGW_ERR_INVALID_ARGUMENT;
+  }
+  int device = 0, sms = 0;
+  if (cudaGetDevice(&device) != cudaSuccess) return FGW_ERR_NO_DEVICE;
+  const int st = device_sm_count_cached(device, &sms);
+  if (st != FGW_OK) return st;
+  const cudaError_t err = launch_wait_selftest(static_cast<WorkspaceHeader*>(workspace),
+                                               static_cast<uint64_t>(budget_ms) * 1000000ull, complete,
+                                               static_cast<cudaStream_t>(stream));
+  return err == cudaSuccess ? FGW_OK : FGW_ERR_CUDA;
+}
+
 int fgw_mha_read_error(const void* workspace, void* stream, int* device_status, int* site) {
   if (workspace == nullptr || device_status == nullptr) return FGW_ERR_INVALID_ARGUMENT;
   if (cudaStreamSynchronize(static_cast<cudaStream_t>(stream)) != cudaSuccess) return FGW_ERR_CUDA;

@@ -227,4 +227,23 @@ cudaError_t launch_merge(const LaunchDesc& d) {
   return cudaGetLastError();
 }
 
+// Failure-detection self-test (fgw_mha_selftest_wait): the library's bounded wait on a phase nobody
+// completes gives up after the budget and records the timeout; nothing traps or faults.
+__global__ void wait_selftest_kernel(WorkspaceHeader* ws, uint64_t budget_ns, int complete) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    ws->error = 0;
+    ws->error_site = 0;
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+    if (complete) mbar_arrive(&bar);
+    if (!mbar_wait(&bar, 0, budget_ns)) record_error(ws, FGW_ERR_DEVICE_TIMEOUT, 99);
+  }
+}
+
+cudaError_t launch_wait_selftest(WorkspaceHeader* ws, uint64_t budget_ns, int complete, cudaStream_t stream) {
+  wait_selftest_kernel<<<1, 32, 0, stream>>>(ws, budget_ns, complete);
+  return cudaGetLastError();
+}
+
 }  // namespace fgw

@@ -59,6 +59,7 @@ void carve_workspace(LaunchDesc& d, void* workspace, int path);
 cudaError_t launch_plan(const LaunchDesc& d);
 cudaError_t launch_decode(const LaunchDesc& d, bool write_partials);
 cudaError_t launch_merge(const LaunchDesc& d);
+cudaError_t launch_wait_selftest(WorkspaceHeader* ws, uint64_t budget_ns, int complete, cudaStream_t stream);
 cudaError_t launch_tensor(const LaunchDesc& d, bool write_partials);
 // Two-query-tile tensor kernel (head_dim <= 128); called by launch_tensor with its tensor maps.
 cudaError_t launch_tensor_pairs(const LaunchDesc& d, bool write_partials, const CUtensorMap& qmap,

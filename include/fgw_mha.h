@@ -168,6 +168,15 @@ FGW_API int fgw_mha_paged_fwd_static_ws(const fgw_mha_params* params, void* stre
  * (FGW_OK or FGW_ERR_DEVICE_TIMEOUT) and which wait site gave up (0 when clean). */
 FGW_API int fgw_mha_read_error(const void* workspace, void* stream, int* device_status, int* site);
 
+/* Self-test of the device-side failure detection (no reference counterpart). One thread clears the
+ * workspace header, then waits, with the same bounded wait every kernel of this library uses, on an
+ * mbarrier phase that nothing completes (complete == 0) or that it completed itself first (complete != 0).
+ * When `budget_ms` runs out the wait records FGW_ERR_DEVICE_TIMEOUT at site 99 and the kernel returns:
+ * no trap, no fault, the context stays usable. Read the outcome with fgw_mha_read_error.
+ * `workspace` needs the 256-byte header only. */
+FGW_API int fgw_mha_selftest_wait(void* workspace, size_t workspace_bytes, int budget_ms, int complete,
+                                  void* stream);
+
 #ifdef __cplusplus
 }
 #endif

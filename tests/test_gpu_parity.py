@@ -99,3 +99,21 @@ def test_device_error_word_clean_after_call():
     kernel(*args, workspace=ws)
     status, site = _native.read_error(ws.data_ptr(), torch.cuda.current_stream().cuda_stream)
     assert (status, site) == (0, 0)
+
+
+def test_bounded_wait_reports_timeout_and_context_survives():
+    # A device wait on a phase nothing completes gives up after its budget and reports
+    # FGW_ERR_DEVICE_TIMEOUT (site 99); the context stays usable for the next forward.
+    import time
+    from fgw_b200 import _native
+    dev = torch.device("cuda", 0)
+    ws = torch.zeros(256, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    t0 = time.perf_counter()
+    _native.selftest_wait(ws.data_ptr(), ws.numel(), 50, False, stream)
+    assert _native.read_error(ws.data_ptr(), stream) == (_native.ERR_DEVICE_TIMEOUT, 99)
+    assert 0.04 < time.perf_counter() - t0 < 5.0
+    _native.selftest_wait(ws.data_ptr(), ws.numel(), 50, True, stream)
+    assert _native.read_error(ws.data_ptr(), stream) == (_native.OK, 0)
+    inputs = build_case(("after_timeout", 1, 130, 1, 128, 128, 2), 7, torch.bfloat16, False, "full")
+    _check(_run(inputs), oracle_output(inputs), inputs)
