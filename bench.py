@@ -15,6 +15,10 @@ Also measured in the same line (``decode``): BASELINE config 5, B256 H32 Q1 KV l
 [1024, 32768], BF16 D128, 64-token pages scattered in a shared pool (~38 GB of K+V), sharded by head
 across the N ranks (strong scaling: whole-box microseconds per call, max over ranks).
 
+And (``gather``): the paged-cache gather pre-pass on the same config-5 pool — both K and V of every
+request packed densely (live lengths rounded up to whole pages, the layout of FGW's gather experiment),
+HBM-bound; the ``attend_after_gather`` field times the decode attention over the packed copy.
+
 ``--impl reference`` times the reference algorithm on the host cores instead: FGW's CPU FP32
 reference restated in NumPy (``oracle/``; the reference itself is Python on an Ascend stack and cannot
 run here), on the same headline workload, rank 0 only.
@@ -50,6 +54,7 @@ def parse_args(argv=None):
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["fgw_b200", "reference"], default="fgw_b200")
     p.add_argument("--no-decode", action="store_true", help="skip the config-5 decode measurement")
+    p.add_argument("--no-gather", action="store_true", help="skip the gather pre-pass measurement")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--path", choices=["auto", "decode", "tensor"], default="auto")
     p.add_argument("--splits", type=int, default=None, help="force num_splits for the headline workload")
@@ -392,7 +397,52 @@ def run_decode(args, rank, world, device, stream):
     err = float(max(np.abs(g - w).max() for g, w in zip(got, want)))
     return {"kernel": kernel, "step_ms": step_ms, "attend_ms": attend_ms, "bytes": nbytes, "per": per,
             "parity": {"requests_checked": len(idx), "max_abs_err": err, "pass": bool(err <= 2e-2)},
-            "launches_per_step": len(fns), "steps": steps}
+            "launches_per_step": len(fns), "steps": steps, "inp": inp, "out": out}
+
+
+def run_gather(args, dc, device, stream):
+    """Paged-cache gather of K and V over the config-5 pool into packed dense buffers, then the decode attention
+    over the packed copy (identity page table, original lengths), against the direct decode's output."""
+    from fgw_b200.operators.mha.current import build_kernel
+    from fgw_b200.operators.mha.paged_cache_gather import packed_layout, paged_cache_gather
+    c = dict(DECODE, batch=args.decode_batch)
+    inp = dc["inp"]
+    heads, page, dim = inp["heads"], c["page"], c["dim"]
+    offsets, rows, table = packed_layout(inp["host_lengths"], page, inp["width"])
+    cu = torch.tensor(offsets, dtype=torch.int32, device=device)
+    dense_table = torch.tensor(table, dtype=torch.int32, device=device)
+    pool_pages = inp["k"].shape[0] // page
+    dense = {n: torch.empty((rows, heads, dim), dtype=torch.bfloat16, device=device) for n in ("k", "v")}
+    caches = {n: inp[n].view(pool_pages, page, heads, dim) for n in ("k", "v")}
+    fns = [(f"gather_{n}", (lambda n=n: paged_cache_gather(dense[n][:offsets[-1]], caches[n], inp["table"], cu)))
+           for n in ("k", "v")]
+    steps = max(5, args.steps // 2)
+    per, totals = timed_steps(fns, steps, max(3, args.warmup // 2), None, stream)
+    gather_ms = sum(totals) / len(totals)
+    nbytes = 2 * 2 * offsets[-1] * heads * dim * 2  # K and V, each read once and written once
+    # exactness: the packed rows of a few requests equal their pool pages
+    exact = True
+    for b in (0, 1, len(offsets) - 2):
+        n_pages = (offsets[b + 1] - offsets[b]) // page
+        ids = inp["table"][b, :n_pages].long()
+        for n in ("k", "v"):
+            want = caches[n][ids].reshape(-1, heads, dim)
+            exact = exact and torch.equal(dense[n][offsets[b]:offsets[b + 1]].view(torch.int16), want.view(torch.int16))
+    kernel = build_kernel(c["batch"], 1, heads, dim, rows, inp["width"], page, False, "bfloat16", device.index,
+                          cache_lengths=tuple(inp["host_lengths"]), path="decode")
+    ws = kernel.new_workspace(device)
+    out = torch.empty_like(inp["q"])
+    a = (inp["q"], dense["k"], dense["v"], dense_table, inp["lengths"])
+    afns = [("plan", lambda: kernel.plan_kernel(*a, ws)), ("attend", lambda: kernel.attend_kernel(*a, ws, out))]
+    if kernel.num_splits > 1:
+        afns.append(("merge", lambda: kernel.merge_only(*a, ws, out)))
+    _, atotals = timed_steps(afns, steps, max(3, args.warmup // 2), None, stream)
+    torch.cuda.synchronize()
+    same = bool(torch.equal(out.view(torch.int16), dc["out"].view(torch.int16)))
+    del dense
+    return {"gather_ms": gather_ms, "bytes": nbytes, "per": per, "exact": bool(exact),
+            "attend_after_gather_ms": sum(atotals) / len(atotals), "same_output_as_direct": same,
+            "packed_rows": offsets[-1], "launches": (len(fns) + len(afns)) * steps}
 
 
 def _pad_pages(t, page):
@@ -564,6 +614,25 @@ def main(argv=None):
                   "stage_ms": {n: statistics.mean(v) for n, v in dc["per"].items()}}
         line["decode"] = decode
         line["gpu_launches"] = line.get("gpu_launches", 0) + decode["gpu_launches"]
+        if not args.no_gather:
+            gt = run_gather(args, dc, device, stream)
+            g_ms = max_over_ranks(gt["gather_ms"], world)
+            achieved = gt["bytes"] / (gt["gather_ms"] * 1e-3) / 1e9
+            line["gather"] = {
+                "workload": f"paged_cache_gather_k_and_v_of_{decode['workload']}", "scaling": "strong",
+                "us_per_call": g_ms * 1e3, "value": sum_over_ranks(gt["bytes"], world) / (g_ms * 1e-3) / 1e9,
+                "unit": "GB/s", "packed_rows_per_rank": gt["packed_rows"],
+                "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                             "frac": achieved / hbm_peak, "kernel": "gather_kernel (two launches: K, V)",
+                             "peak_source": f"{peak_kind} hbm_gbs"},
+                "exact_rows": gt["exact"],
+                "attend_after_gather_us": max_over_ranks(gt["attend_after_gather_ms"], world) * 1e3,
+                "gather_plus_attend_us": (g_ms + max_over_ranks(gt["attend_after_gather_ms"], world)) * 1e3,
+                "direct_attend_us": step_ms * 1e3,
+                "same_output_as_direct": gt["same_output_as_direct"],
+                "gpu_launches": gt["launches"]}
+            line["gpu_launches"] += gt["launches"]
+        del dc
         if lq is None:
             line.update({"value": decode["value"], "unit": "GB/s", "ms_per_step": step_ms, "vs_baseline": None,
                          "config": {"workload": decode["workload"]}, "roofline": decode["roofline"]})

@@ -20,6 +20,7 @@ ERR_NO_DEVICE = 6
 
 DTYPE_FLOAT16 = 0
 DTYPE_BFLOAT16 = 1
+DTYPE_FLOAT8_E4M3 = 2  # paged-cache gather only
 
 PATH_AUTO = 0
 PATH_DECODE = 1
@@ -30,7 +31,7 @@ SCHEDULE_AUTO = 0
 SCHEDULE_STRIDED = 1
 SCHEDULE_CONTIGUOUS = 2
 
-ABI_VERSION = 2  # FGW_MHA_ABI_VERSION the Params layout below matches
+ABI_VERSION = 3  # FGW_MHA_ABI_VERSION the Params / GatherParams layouts below match
 
 EXPORTED = (
     "fgw_mha_abi_version",
@@ -46,6 +47,7 @@ EXPORTED = (
     "fgw_mha_read_error",
     "fgw_mha_paged_fwd_static_ws",
     "fgw_mha_selftest_wait",
+    "fgw_paged_cache_gather",
 )
 
 STATIC_WORKSPACE_BYTES = 16 << 20  # FGW_MHA_STATIC_WORKSPACE_BYTES
@@ -87,6 +89,28 @@ class Params(ctypes.Structure):
         ("path", ctypes.c_int32),
         ("wait_budget_ms", ctypes.c_int32),
         ("schedule", ctypes.c_int32),
+        ("reserved", ctypes.c_int32 * 3),
+    ]
+
+
+class GatherParams(ctypes.Structure):
+    """Mirror of ``fgw_gather_params`` (include/fgw_mha.h)."""
+
+    _fields_ = [
+        ("dst", ctypes.c_void_p),
+        ("cache", ctypes.c_void_p),
+        ("block_table", ctypes.c_void_p),
+        ("cu_seq_lens", ctypes.c_void_p),
+        ("seq_starts", ctypes.c_void_p),
+        ("scale", ctypes.c_void_p),
+        ("total_rows", ctypes.c_int64),
+        ("batch", ctypes.c_int32),
+        ("num_pages", ctypes.c_int32),
+        ("page_size", ctypes.c_int32),
+        ("table_width", ctypes.c_int32),
+        ("row_width", ctypes.c_int32),
+        ("dtype", ctypes.c_int32),
+        ("out_dtype", ctypes.c_int32),
         ("reserved", ctypes.c_int32 * 3),
     ]
 
@@ -136,6 +160,8 @@ def library():
     lib.fgw_mha_selftest_wait.restype = ctypes.c_int
     lib.fgw_mha_paged_fwd_static_ws.argtypes = [p, vp]
     lib.fgw_mha_paged_fwd_static_ws.restype = ctypes.c_int
+    lib.fgw_paged_cache_gather.argtypes = [ctypes.POINTER(GatherParams), vp]
+    lib.fgw_paged_cache_gather.restype = ctypes.c_int
     _LIB = lib
     return lib
 
@@ -216,3 +242,9 @@ def selftest_wait(workspace_ptr, workspace_bytes, budget_ms, complete, stream_pt
 def paged_fwd_static_ws(params, stream_ptr):
     """Forward with the library's own static scratch array: allocates nothing (see include/fgw_mha.h)."""
     check(library().fgw_mha_paged_fwd_static_ws(ctypes.byref(params), stream_ptr), "fgw_mha_paged_fwd_static_ws")
+
+
+def paged_cache_gather(params, stream_ptr):
+    """``fgw_paged_cache_gather``: pack the cache rows the requests reach into ``params.dst``."""
+    check(library().fgw_paged_cache_gather(ctypes.byref(params), ctypes.c_void_p(stream_ptr)),
+          "fgw_paged_cache_gather")

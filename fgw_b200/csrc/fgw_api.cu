@@ -317,6 +317,18 @@ int fgw_mha_selftest_wait(void* workspace, size_t workspace_bytes, int budget_ms
   return err == cudaSuccess ? FGW_OK : FGW_ERR_CUDA;
 }
 
+int fgw_paged_cache_gather(const fgw_gather_params* params, void* stream) {
+  if (params == nullptr) return FGW_ERR_INVALID_ARGUMENT;
+  int st = gather_validate(*params);
+  if (st != FGW_OK || params->total_rows == 0) return st;
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess) return FGW_ERR_NO_DEVICE;
+  int sms = 0;
+  st = device_sm_count_cached(device, &sms);
+  if (st != FGW_OK) return st;
+  return launch_gather(*params, sms, static_cast<cudaStream_t>(stream)) == cudaSuccess ? FGW_OK : FGW_ERR_CUDA;
+}
+
 int fgw_mha_read_error(const void* workspace, void* stream, int* device_status, int* site) {
   if (workspace == nullptr || device_status == nullptr) return FGW_ERR_INVALID_ARGUMENT;
   if (cudaStreamSynchronize(static_cast<cudaStream_t>(stream)) != cudaSuccess) return FGW_ERR_CUDA;

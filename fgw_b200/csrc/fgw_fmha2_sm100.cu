@@ -673,7 +673,9 @@ __global__ void __launch_bounds__(384, 1)
           __threadfence();
           if (warp == 4 && lane == 0) a.counters[sg.item] = 0;  // ready for the next launch
           // base-2 LSE merge (the split merge's arithmetic, merge_kernel in fgw_aux.cu); own piece from TMEM.
-          // Every lane runs the TMEM loads (warp-collective); only valid rows touch global memory.
+          // The pieces are combined in piece order whichever of them merges (its own normalised O and LSE are
+          // the values it would have written to its slot), so the result does not depend on which CTA
+          // finished last. Every lane runs the TMEM loads (warp-collective); only valid rows touch global memory.
           float peak = own_lse;
           float wsum = 0.f;
           if (row_valid) {
@@ -681,35 +683,40 @@ __global__ void __launch_bounds__(384, 1)
               if (k != own) peak = fmaxf(peak, __ldcg(&a.slot_lse[piece_row(k)]));
             }
             for (int k = 0; k < pieces; ++k) {
-              if (k == own) continue;
-              const float lse = __ldcg(&a.slot_lse[piece_row(k)]);
+              const float lse = k == own ? own_lse : __ldcg(&a.slot_lse[piece_row(k)]);
               if (lse > kValidLse) wsum += fast_exp2(lse - peak);
             }
           }
-          const float w_own = own_lse > kValidLse ? fast_exp2(own_lse - peak) : 0.f;
-          wsum += w_own;
           const float scale = wsum > 0.f ? 1.f / wsum : 0.f;
           for (int cb = 0; cb < D / 16; ++cb) {
-            float acc[16];
-            load_o(cb, acc);  // warp-collective: every lane, valid row or not
+            float mine[16];
+            load_o(cb, mine);  // warp-collective: every lane, valid row or not
             if (row_valid) {
+              float acc[16];
 #pragma unroll
-              for (int i = 0; i < 16; ++i) acc[i] *= w_own;
+              for (int i = 0; i < 16; ++i) acc[i] = 0.f;
               for (int k = 0; k < pieces; ++k) {
-                if (k == own) continue;
                 const long long pr = piece_row(k);
-                const float lse = __ldcg(&a.slot_lse[pr]);
+                const float lse = k == own ? own_lse : __ldcg(&a.slot_lse[pr]);
                 if (!(lse > kValidLse)) continue;
                 const float w = fast_exp2(lse - peak);
-                const float4* src = reinterpret_cast<const float4*>(a.slot_o + pr * D + cb * 16);
+                float v[16];
+                if (k == own) {
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                  const float4 v = __ldcg(src + i);
-                  acc[4 * i] += w * v.x;
-                  acc[4 * i + 1] += w * v.y;
-                  acc[4 * i + 2] += w * v.z;
-                  acc[4 * i + 3] += w * v.w;
+                  for (int i = 0; i < 16; ++i) v[i] = mine[i];
+                } else {
+                  const float4* src = reinterpret_cast<const float4*>(a.slot_o + pr * D + cb * 16);
+#pragma unroll
+                  for (int i = 0; i < 4; ++i) {
+                    const float4 x = __ldcg(src + i);
+                    v[4 * i] = x.x;
+                    v[4 * i + 1] = x.y;
+                    v[4 * i + 2] = x.z;
+                    v[4 * i + 3] = x.w;
+                  }
                 }
+#pragma unroll
+                for (int i = 0; i < 16; ++i) acc[i] = fmaf(w, v[i], acc[i]);
               }
               store_row(cb, acc, scale);
             }

@@ -56,6 +56,9 @@ size_t workspace_bytes(const fgw_mha_params& p, int path);
 void carve_workspace(LaunchDesc& d, void* workspace, int path);
 
 // Kernel launchers (return a cudaError_t from the launch).
+// Paged-cache gather (fgw_gather.cu): argument check (an fgw_status) and launch.
+int gather_validate(const fgw_gather_params& p);
+cudaError_t launch_gather(const fgw_gather_params& p, int sm_count, cudaStream_t stream);
 cudaError_t launch_plan(const LaunchDesc& d);
 cudaError_t launch_decode(const LaunchDesc& d, bool write_partials);
 cudaError_t launch_merge(const LaunchDesc& d);

@@ -22,6 +22,10 @@
  *                           (v7_experimental.py:842-855: direct_kernel / partial_kernel / merge_kernel).
  *   fgw_mha_device_sm_count the core count the reference reads from the device properties
  *                           (v7.py:65-68, 104-107 `cube_core_num`).
+ *   fgw_paged_cache_gather  the paged-cache gather pre-pass FGW pins from TileOPs and runs before attention
+ *                           in its gather experiment: third_party/tileops_yyttt6/paged_cache_gather.py:108-232
+ *                           (`_compile`), :44-104 (`_compile_generic`), :264-296 (`forward`); call site
+ *                           benchmarks/mha/external_cache_gather.py:38-58.
  */
 #ifndef FGW_MHA_H_
 #define FGW_MHA_H_
@@ -33,7 +37,7 @@
 extern "C" {
 #endif
 
-#define FGW_MHA_ABI_VERSION 2
+#define FGW_MHA_ABI_VERSION 3
 
 #if defined(__GNUC__)
 #define FGW_API __attribute__((visibility("default")))
@@ -51,7 +55,9 @@ typedef enum fgw_status {
   FGW_ERR_NO_DEVICE = 6            /* no sm_100 device is current */
 } fgw_status;
 
-typedef enum fgw_dtype { FGW_DTYPE_FLOAT16 = 0, FGW_DTYPE_BFLOAT16 = 1 } fgw_dtype;
+/* Element types. The attention entry points take FLOAT16 / BFLOAT16; FLOAT8_E4M3 is a cache type of the
+ * paged-cache gather only (fgw_paged_cache_gather). */
+typedef enum fgw_dtype { FGW_DTYPE_FLOAT16 = 0, FGW_DTYPE_BFLOAT16 = 1, FGW_DTYPE_FLOAT8_E4M3 = 2 } fgw_dtype;
 
 /* Which kernel family runs the QK^T -> softmax -> PV body. */
 typedef enum fgw_path {
@@ -176,6 +182,36 @@ FGW_API int fgw_mha_read_error(const void* workspace, void* stream, int* device_
  * `workspace` needs the 256-byte header only. */
 FGW_API int fgw_mha_selftest_wait(void* workspace, size_t workspace_bytes, int budget_ms, int complete,
                                   void* stream);
+
+/*
+ * Paged-cache gather: packs the cache rows that requests reach, in request order, into a dense buffer.
+ * Output row r of request i (cu_seq_lens[i] <= r < cu_seq_lens[i + 1]) is the cache row
+ *   block_table[i, pos / page_size] * page_size + pos % page_size,   pos = r - cu_seq_lens[i] + seq_starts[i]
+ * (seq_starts NULL: 0). FLOAT16/BFLOAT16 rows are copied bit for bit (out_dtype == dtype); FLOAT8_E4M3 rows
+ * become round_to_nearest(float(code) * scale[0]) in out_dtype (FLOAT16 or BFLOAT16). Rows before
+ * cu_seq_lens[0] or from cu_seq_lens[batch] on, positions below 0 or past the table, and page ids outside
+ * [0, num_pages) are written as zeros (the reference leaves them undefined); nothing is read out of bounds.
+ * Offsets, starts, page ids and the scale stay device data. Asynchronous on `stream`.
+ */
+typedef struct fgw_gather_params {
+  void* dst;                   /* [total_rows, row_width] out_dtype, contiguous, written */
+  const void* cache;           /* [num_pages * page_size, row_width] dtype, contiguous, read-only */
+  const int32_t* block_table;  /* [batch, table_width] physical page ids */
+  const int32_t* cu_seq_lens;  /* [batch + 1] first output row of every request (non-decreasing) */
+  const int32_t* seq_starts;   /* [batch] first logical position of every request, or NULL */
+  const float* scale;          /* [1] dequantisation scale, FLOAT8_E4M3 caches only (NULL otherwise) */
+  int64_t total_rows;          /* output rows (normally cu_seq_lens[batch]) */
+  int32_t batch;
+  int32_t num_pages;
+  int32_t page_size;
+  int32_t table_width;
+  int32_t row_width;           /* elements per cache row (e.g. heads * head_dim) */
+  int32_t dtype;               /* fgw_dtype of the cache */
+  int32_t out_dtype;           /* fgw_dtype of dst: dtype, or FLOAT16/BFLOAT16 for an FP8 cache */
+  int32_t reserved[3];         /* must be zero */
+} fgw_gather_params;
+
+FGW_API int fgw_paged_cache_gather(const fgw_gather_params* params, void* stream);
 
 #ifdef __cplusplus
 }

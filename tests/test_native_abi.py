@@ -15,7 +15,7 @@ HEADER = pathlib.Path(__file__).resolve().parent.parent / "include" / "fgw_mha.h
 
 def declared_functions():
     text = HEADER.read_text(encoding="utf-8")
-    return sorted(set(re.findall(r"FGW_API\s+[\w\s\*]*?\b(fgw_mha_\w+)\s*\(", text)))
+    return sorted(set(re.findall(r"FGW_API\s+[\w\s\*]*?\b(fgw_\w+)\s*\(", text)))
 
 
 def test_header_declares_the_exported_set():
@@ -26,7 +26,7 @@ def test_library_loads_and_exports_every_declared_symbol():
     lib = _native.library()
     for name in declared_functions():
         assert hasattr(lib, name), name
-    assert _native.abi_version() == _native.ABI_VERSION == 2
+    assert _native.abi_version() == _native.ABI_VERSION == 3
 
 
 def test_status_strings():
@@ -102,3 +102,42 @@ def test_null_pointers_rejected():
 def test_resolve_path_respects_explicit_choice():
     assert _native.resolve_path(_params(path=_native.PATH_DECODE)) == _native.PATH_DECODE
     assert _native.resolve_path(_params(path=_native.PATH_TENSOR)) == _native.PATH_TENSOR
+
+
+def test_gather_params_layout_matches_header():
+    # six pointers, int64 total_rows, seven int32 fields (the last is out_dtype) + 3 reserved
+    assert _native.GatherParams.total_rows.offset == 6 * 8
+    assert _native.GatherParams.out_dtype.offset == 6 * 8 + 8 + 6 * 4
+    assert ctypes.sizeof(_native.GatherParams) == 6 * 8 + 8 + 10 * 4
+
+
+def _gather(**overrides):
+    g = _native.GatherParams()
+    for key, value in dict(total_rows=0, batch=2, num_pages=8, page_size=16, table_width=4, row_width=256,
+                           dtype=_native.DTYPE_BFLOAT16, out_dtype=_native.DTYPE_BFLOAT16).items():
+        setattr(g, key, value)
+    for key, value in overrides.items():
+        setattr(g, key, value)
+    return g
+
+
+def _gather_status(g):
+    return _native.library().fgw_paged_cache_gather(ctypes.byref(g), None)
+
+
+def test_gather_argument_checks_without_a_device():
+    # an empty gather is a no-op that never touches the device
+    assert _gather_status(_gather()) == _native.OK
+    bad = [dict(batch=0), dict(page_size=0), dict(row_width=0), dict(total_rows=-1),
+           dict(out_dtype=_native.DTYPE_FLOAT16),                          # unquantized gather keeps the type
+           dict(dtype=_native.DTYPE_FLOAT8_E4M3),                          # FP8 needs a scale
+           dict(dtype=_native.DTYPE_FLOAT8_E4M3, out_dtype=_native.DTYPE_FLOAT8_E4M3, scale=8),
+           dict(scale=8),                                                 # a scale only goes with FP8
+           dict(page_size=1 << 20, table_width=1 << 12),                  # positions must fit int32
+           dict(dtype=7), dict(total_rows=5)]                             # rows to write but no pointers
+    for overrides in bad:
+        g = _gather(**overrides)
+        assert _gather_status(g) == _native.ERR_INVALID_ARGUMENT, overrides
+    g = _gather()
+    g.reserved[1] = 1
+    assert _gather_status(g) == _native.ERR_INVALID_ARGUMENT
