@@ -618,12 +618,19 @@ def main(argv=None):
             gt = run_gather(args, dc, device, stream)
             g_ms = max_over_ranks(gt["gather_ms"], world)
             achieved = gt["bytes"] / (gt["gather_ms"] * 1e-3) / 1e9
+            g_traffic = None
+            prof = ROOT / "profiles" / "traffic_per_launch.json"
+            if prof.exists():
+                per_row = json.loads(prof.read_text()).get("gather_bytes_per_packed_row")
+                if per_row:
+                    g_traffic = per_row * gt["packed_rows"]  # one launch (one cache)
             line["gather"] = {
                 "workload": f"paged_cache_gather_k_and_v_of_{decode['workload']}", "scaling": "strong",
                 "us_per_call": g_ms * 1e3, "value": sum_over_ranks(gt["bytes"], world) / (g_ms * 1e-3) / 1e9,
                 "unit": "GB/s", "packed_rows_per_rank": gt["packed_rows"],
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                              "frac": achieved / hbm_peak, "kernel": "gather_kernel (two launches: K, V)",
+                             "traffic": g_traffic, "traffic_unit": "bytes per launch",
                              "peak_source": f"{peak_kind} hbm_gbs"},
                 "exact_rows": gt["exact"],
                 "attend_after_gather_us": max_over_ranks(gt["attend_after_gather_ms"], world) * 1e3,
