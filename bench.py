@@ -621,9 +621,9 @@ def main(argv=None):
             g_traffic = None
             prof = ROOT / "profiles" / "traffic_per_launch.json"
             if prof.exists():
-                per_row = json.loads(prof.read_text()).get("gather_bytes_per_packed_row")
-                if per_row:
-                    g_traffic = per_row * gt["packed_rows"]  # one launch (one cache)
+                ratio = json.loads(prof.read_text()).get("gather_traffic_per_algorithmic_byte")
+                if ratio:
+                    g_traffic = ratio * gt["bytes"] / 2  # one launch (one cache) of this rank
             line["gather"] = {
                 "workload": f"paged_cache_gather_k_and_v_of_{decode['workload']}", "scaling": "strong",
                 "us_per_call": g_ms * 1e3, "value": sum_over_ranks(gt["bytes"], world) / (g_ms * 1e-3) / 1e9,
