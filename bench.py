@@ -55,6 +55,8 @@ def parse_args(argv=None):
     p.add_argument("--impl", choices=["fgw_b200", "reference"], default="fgw_b200")
     p.add_argument("--no-decode", action="store_true", help="skip the config-5 decode measurement")
     p.add_argument("--no-gather", action="store_true", help="skip the gather pre-pass measurement")
+    p.add_argument("--sweep-splits", default=None, metavar="JSON",
+                   help="run the config-3 split sweep instead, write its rows to JSON and print a summary line")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--path", choices=["auto", "decode", "tensor"], default="auto")
     p.add_argument("--splits", type=int, default=None, help="force num_splits for the headline workload")
@@ -500,6 +502,76 @@ def cpu_longq_sample(budget_s=12.0):
 
 
 # ---------------------------------------------------------------------------------------- reference arm
+SWEEP = dict(shapes=((1, 1), (2, 8)), dtypes=("float16", "bfloat16"), queries=(1, 4, 16, 64, 512),
+             kvs=(512, 2048, 8192, 32768), splits=(1, 2, 4, 8, 16, 32), dim=128, page=128)
+
+
+def run_split_sweep(args, device, stream):
+    """Config 3: every (B, H) x dtype x Q x KV of the reference's split sweep, full caches, page 128, N(0,1)
+    data; for each split count the call accepts, the median of 5 timings of 20 calls replayed from a CUDA
+    graph (plan + attend + merge; warm L2, as the reference's scan). Rows in the split-model fitter's format."""
+    from fgw_b200.operators.mha.current import build_kernel
+    c = SWEEP
+    rows = []
+    for (b, h) in c["shapes"]:
+        for kv in c["kvs"]:
+            width = kv // c["page"]
+            g = torch.Generator(device=device).manual_seed(31 + b + kv)
+            pool = b * width
+            table = torch.randperm(pool, device=device, generator=g)[:pool].reshape(b, width).int()
+            lengths = torch.full((b,), kv, dtype=torch.int32, device=device)
+            kf = torch.randn(pool * c["page"], h, c["dim"], device=device, generator=g)
+            vf = torch.randn(pool * c["page"], h, c["dim"], device=device, generator=g)
+            for dtype in c["dtypes"]:
+                tdtype = getattr(torch, dtype)
+                k, v = kf.to(tdtype), vf.to(tdtype)
+                for sq in c["queries"]:
+                    q = torch.randn(b, sq, h, c["dim"], device=device, generator=g).to(tdtype)
+                    # FP16 takes the general route (the default FP16 route accepts no explicit split count)
+                    mode = "general" if dtype == "float16" else "stable"
+                    auto = build_kernel(b, sq, h, c["dim"], pool * c["page"], width, c["page"], False, dtype,
+                                        device.index, full_kv_cache=True, cache_lengths=(kv,) * b, cube_mode=mode)
+                    median = {}
+                    for splits in c["splits"]:
+                        try:
+                            kernel = build_kernel(b, sq, h, c["dim"], pool * c["page"], width, c["page"], False,
+                                                  dtype, device.index, num_splits=splits, full_kv_cache=True,
+                                                  cube_mode=mode)
+                        except ValueError:
+                            continue  # more splits than KV tiles, or a split count this route does not take
+                        ws = kernel.new_workspace(device)
+                        out = torch.empty_like(q)
+                        a = (q, k, v, table, lengths)
+                        for _ in range(3):
+                            kernel(*a, out=out, workspace=ws)
+                        torch.cuda.synchronize()
+                        graph = torch.cuda.CUDAGraph()
+                        with torch.cuda.graph(graph):
+                            for _ in range(20):
+                                kernel(*a, out=out, workspace=ws)
+                        times = []
+                        for _ in range(6):
+                            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                            e0.record(stream)
+                            graph.replay()
+                            e1.record(stream)
+                            torch.cuda.synchronize()
+                            times.append(e0.elapsed_time(e1) * 1e3 / 20)
+                        median[str(splits)] = statistics.median(times[1:])
+                        del graph
+                    if not median:
+                        continue
+                    best = min(median, key=median.get)
+                    rows.append({"case": f"B{b}H{h}_Q{sq}_KV{kv}", "key": f"B{b}H{h}_Q{sq}_KV{kv}_{dtype}",
+                                 "B": b, "Q": sq, "H": h, "D": c["dim"], "dtype": dtype, "page_size": c["page"],
+                                 "table_width": width, "lengths": [kv] * b, "median_us": median,
+                                 "auto_num_splits": auto.num_splits, "split_policy": auto.split_policy,
+                                 "best_num_splits": int(best),
+                                 "auto_relative_to_best": median.get(str(auto.num_splits), float("nan"))
+                                 / median[best]})
+    return rows
+
+
 def reference_arm(args, rank, world):
     if rank != 0:
         return 0
@@ -555,6 +627,16 @@ def main(argv=None):
     init_dist(world, local)
     device = torch.device("cuda", local)
     stream = torch.cuda.current_stream(device)
+    if args.sweep_splits:
+        rows = run_split_sweep(args, device, stream)
+        pathlib.Path(args.sweep_splits).write_text(json.dumps({"rows": rows, "gpu": torch.cuda.get_device_name(device),
+                                                               "source_precision_us": 0.001}, indent=1) + "\n")
+        ratios = [r["auto_relative_to_best"] for r in rows]
+        print(json.dumps({"sweep": "config3_split_sweep", "cases": len(rows),
+                          "auto_within_2pct": sum(x <= 1.02 for x in ratios),
+                          "auto_geomean_relative_to_best": math.exp(sum(math.log(x) for x in ratios) / len(ratios)),
+                          "auto_max_relative_to_best": max(ratios), "rows_file": args.sweep_splits}), flush=True)
+        return 0
     hbm_peak, tc_peak, peak_kind = measured_peaks()
     line = {"metric": METRIC, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "higher_is_better": True, "scaling": "weak", "dtype": "bf16", "data": "synthetic"}

@@ -11,7 +11,15 @@ Restates ``operators/mha/general_split_cost_model.py:44-91`` of FGW:
 
 ``cores=28`` with the reference coefficients (``models/reference_general_split_cost_model_v*.json``)
 reproduces the reference bit for bit; the reference's constants 28 and 56 are ``cores`` and
-``2 * cores``. B200 uses ``cores`` = the SM count and ``models/b200_general_split_cost_model.json``.
+``2 * cores``.
+
+Version 3 is the B200 feature set (no reference counterpart), fitted on B200 split sweeps with the
+reference's method (``fit_split_cost_model.py``) into ``models/b200_general_split_cost_model.json``. It
+describes the B200 kernels instead of the Ascend ones: query rows per work item are the decode kernel's
+(``decode_rows``) for up to 8 query rows and 256-row pairs above, KV tiles have 128 tokens, serial work
+per program is counted separately for the two kernels, and with one split a tensor-path launch whose items
+fill fewer than 2/3 of the programs runs the contiguous schedule (KV tiles spread evenly over the
+programs).
 """
 import functools
 import json
@@ -27,17 +35,64 @@ FEATURE_NAMES = (
     "partial_tasks_times_splits_times_padded_d",
 )
 FEATURE_NAMES_V2 = FEATURE_NAMES + ("longest_partition_excess_times_padded_d", "longest_partition_excess")
+FEATURE_NAMES_V3 = (
+    "constant", "decode_serial_tiles", "tensor_serial_tiles", "decode_waves", "tensor_waves", "has_merge",
+    "splits", "merge_rows_times_splits", "longest_partition_excess", "contiguous_pieces_per_item",
+)
+DECODE_MAX_QUERIES = 8  # query rows per request at or below which the decode kernel runs
+PAIR_ROWS = 256         # query rows per tensor-path work item (two 128-row tiles)
+KV_TILE = 128
 
 
 def model_path(version=1):
-    if type(version) is not int or version not in (1, 2):
-        raise ValueError("General model version must be1 or2")
+    if type(version) is not int or version not in (1, 2, 3):
+        raise ValueError("General model version must be 1, 2 or 3")
+    if version == 3:
+        return MODEL_DIR / "b200_general_split_cost_model.json"
     return MODEL_DIR / f"reference_general_split_cost_model_v{version}.json"
 
 
 def feature_names(version=1):
     model_path(version)
-    return FEATURE_NAMES if version == 1 else FEATURE_NAMES_V2
+    return {1: FEATURE_NAMES, 2: FEATURE_NAMES_V2, 3: FEATURE_NAMES_V3}[version]
+
+
+def decode_rows(dim):
+    """Query rows per decode work item (DecodeShape<D>::kRows of the decode kernel)."""
+    chunks = dim // 8
+    lanes = 8 if chunks >= 8 else (4 if chunks >= 4 else 2)
+    per_lane = -(-chunks // lanes) * 8
+    return 1 if per_lane >= 32 else (2 if per_lane >= 16 else 4)
+
+
+def _features_b200(batch, sq, heads, dim, lengths, splits, cores):
+    tiles = [(n + KV_TILE - 1) // KV_TILE for n in lengths]
+    mean_tiles = sum(tiles) / batch
+    decode = sq <= DECODE_MAX_QUERIES
+    rows = decode_rows(dim) if decode else PAIR_ROWS
+    items = batch * heads * ((sq + rows - 1) // rows) * splits
+    pieces = 0.0
+    if not decode and splits == 1 and 3 * items < 2 * min(cores, 148):
+        programs = min(cores, 148)
+        serial = math.ceil(items * max(mean_tiles, 1.0) / programs)
+        waves = 1
+        # an item cut into this many pieces is merged by one CTA (it reads every other piece's partial rows)
+        pieces = min(programs / items, max(mean_tiles, 1.0))
+    else:
+        waves = (items + cores - 1) // cores
+        serial = waves * math.ceil(mean_tiles / splits)
+    longest = (max(tiles) + splits - 1) // splits
+    multi = 1 if splits > 1 else 0
+    return [1.0,
+            float(serial) if decode else 0.0,
+            0.0 if decode else float(serial),
+            float(waves) if decode else 0.0,
+            0.0 if decode else float(waves),
+            float(multi),
+            float(splits),
+            multi * batch * heads * sq * splits / cores,
+            max(0.0, longest - mean_tiles / splits),
+            pieces]
 
 
 @functools.lru_cache(maxsize=8)
@@ -60,6 +115,8 @@ def features(batch, sq, heads, dim, lengths, splits, version=1, cores=28):
         raise ValueError("One nonnegative integer cache length per request required")
     if type(splits) is not int or splits not in SPLITS:
         raise ValueError("Unsupported split count")
+    if version == 3:
+        return _features_b200(batch, sq, heads, dim, lengths, splits, cores)
     padded_d = max(32, 1 << (dim - 1).bit_length()) / 64
     tasks = batch * heads * ((sq + 31) // 32)
     waves = (tasks * splits + cores - 1) // cores
@@ -100,7 +157,9 @@ def select_model_splits(batch, sq, heads, dim, page_size, width, lengths, model=
     if len(lengths) != batch or any(n > page_size * width for n in lengths):
         raise ValueError("cache_lengths must match batch and page-table capacity")
     model = load_model(version) if model is None else model
-    capacity_tiles = (page_size * width + 31) // 32
+    # KV tiles of table capacity: 32-token tiles of the reference's general kernel; 128 on B200 (version 3)
+    tile = KV_TILE if model["version"] == 3 else 32
+    capacity_tiles = (page_size * width + tile - 1) // tile
     costs = {}
     for s in SPLITS:
         if s <= capacity_tiles:

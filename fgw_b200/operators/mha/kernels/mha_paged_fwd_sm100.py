@@ -82,11 +82,11 @@ def _dtype_code(dtype):
 def _b200_model(name):
     if name == "v7":
         return v7_model.load_model(v7_model.B200_MODEL)
-    return general_model.load_model(2, str(general_model.MODEL_DIR / "b200_general_split_cost_model.json"))
+    return general_model.load_model(3)  # the B200 feature set fitted on B200 split sweeps
 
 
 def _select_auto_splits(batch, sq, heads, dim, width, page_size, lengths, cores):
-    """B200 split choice from host-known lengths (or table capacity) with the general model forms."""
+    """B200 split choice from host-known lengths (or table capacity) with the fitted B200 model."""
     if lengths is None:
         lengths = (width * page_size,) * batch
     return general_model.select_model_splits(batch, sq, heads, dim, page_size, width, list(lengths),
@@ -146,6 +146,12 @@ def build_kernel(batch, sq, heads, dim, pool_rows, width, page_size, causal, dty
                 raise ValueError("Experimental cost model requires host-known cache_lengths")
             splits = general_model.select_model_splits(batch, sq, heads, dim, page_size, width, list(cache_lengths),
                                                        model=_b200_model("general"), cores=cores)
+            policy_name = "cost_model"
+        elif num_splits is None and split_policy == "auto":
+            # The reference's rule here fills the cores (fill_28); over 148 SMs that over-splits (the config-3
+            # sweep measured it 1.2-2.4x slower than the best split), so "auto" takes the fitted B200 model,
+            # over table capacity when the lengths are not known on the host.
+            splits = _select_auto_splits(batch, sq, heads, dim, width, page_size, cache_lengths, cores)
             policy_name = "cost_model"
         else:
             splits = general_policy.select_splits(tasks, capacity_tiles, num_splits, target_programs=cores)

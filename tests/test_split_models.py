@@ -68,7 +68,52 @@ def test_b200_models_load_and_choose_valid_splits():
     assert b200["cores"] == 148
     s = sm.select_splits(2, 4096, 8, 16, model=b200)
     assert s in sm.SPLITS
-    general = gm.load_model(2, str(gm.MODEL_DIR / "b200_general_split_cost_model.json"))
+    general = gm.load_model(3)
     for lengths in ([2048], [1024] * 256, [0, 32768]):
         s = gm.select_model_splits(len(lengths), 1, 32, 128, 64, 512, lengths, model=general, cores=148)
         assert s in gp.SPLITS
+
+
+def _sweep():
+    import json
+    import pathlib
+    return json.loads((pathlib.Path(__file__).resolve().parent / "golden" / "b200_split_sweep.json").read_text())
+
+
+def test_b200_model_is_the_fit_of_the_committed_sweep():
+    # fit_split_cost_model restates FGW's fitter (tools/mha/fit_general_split_model.py); refitting the
+    # committed B200 sweep reproduces the shipped model and its validation
+    from fgw_b200.operators.mha.fit_split_cost_model import fit_and_validate
+    shipped = gm.load_model(3)
+    model = fit_and_validate(_sweep()["rows"], version=3, cores=148)
+    assert model["weights"] == pytest.approx(shipped["weights"], rel=1e-6, abs=1e-9)
+    assert model["latency_floor_us"] == shipped["latency_floor_us"]
+    loso = model["validation"]["leave_one_shape_out"]
+    assert loso["geomean_regret_percent"] < 5 and loso["max_regret_percent"] < 30 and loso["within_2pct"] >= 55
+
+
+def test_b200_features_by_hand():
+    # decode path (Q <= 8): D128 items carry 2 query rows; 2048 tokens = 16 tiles of 128
+    f = gm.features(1, 1, 1, 128, [2048], 4, version=3, cores=148)
+    assert f == [1.0, 4.0, 0.0, 1.0, 0.0, 1.0, 4.0, 4 / 148, 0.0, 0.0]
+    # tensor path, one split, few items: the contiguous schedule spreads 16 tiles over 148 programs
+    f = gm.features(1, 16, 1, 128, [2048], 1, version=3, cores=148)
+    assert f == [1.0, 0.0, 1.0, 0.0, 1.0, 0.0, 1.0, 0.0, 0.0, 16.0]
+    # tensor path, 2 x 8 heads x 2 query pairs x 4 splits = 128 items in one wave
+    f = gm.features(2, 512, 8, 128, [4096, 2048], 4, version=3, cores=148)
+    assert f[2] == 6.0 and f[4] == 1.0 and f[8] == 8 - 6.0
+    with pytest.raises(ValueError):
+        gm.features(1, 1, 1, 128, [2048], 3, version=3)
+
+
+def test_b200_model_selection_on_the_sweep():
+    model = gm.load_model(3)
+    rows = _sweep()["rows"]
+    regret = []
+    for r in rows:
+        if "32" in r["median_us"] or r["B"] == 2:  # splits the route measured
+            pick = gm.select_model_splits(r["B"], r["Q"], r["H"], r["D"], r["page_size"], r["table_width"],
+                                          list(r["lengths"]), model=model)
+            if str(pick) in r["median_us"]:
+                regret.append(r["median_us"][str(pick)] / min(r["median_us"].values()))
+    assert len(regret) > 40 and max(regret) < 1.5
