@@ -175,6 +175,7 @@ __global__ void __launch_bounds__(DecodeShape<D>::kThreads, 1)
     const int tiles = (end_tok + S::kTile - 1) / S::kTile;
     const int t_begin = (int)((long long)tiles * s / a.splits);
     const int t_end = (int)((long long)tiles * (s + 1) / a.splits);
+    const int nrows = min(kRows, a.sq - q0);  // query rows of this item that exist
 
     // Query rows for this lane's chunks, pre-scaled into the base-2 score domain.
     float qv[kRows][S::kCpl * 8];
@@ -217,17 +218,21 @@ __global__ void __launch_bounds__(DecodeShape<D>::kThreads, 1)
         const T* ktile = ring + (size_t)stage * (2 * S::kTile * D);
         const T* vtile = ktile + S::kTile * D;
         const int tok0 = t * S::kTile;
-#pragma unroll 1
+        // Scores of this group's kTpg tokens of the tile, computed independently (each dot product in four
+        // partial sums), then one max / rescale per tile, then the V rows (each loaded once for every query
+        // row). Tokens at or past end_tok are never used: their shared-memory rows were not loaded.
+        float sc[S::kTpg][kRows];
+        bool live[S::kTpg];
+#pragma unroll
         for (int j = 0; j < S::kTpg; ++j) {
           const int tt = group + j * S::kGroups;
-          const int tok = tok0 + tt;
-          if (tok >= end_tok) break;  // uniform within the group
+          live[j] = tok0 + tt < end_tok;  // uniform within the group
           float kf[S::kCpl * 8];
 #pragma unroll
           for (int c = 0; c < S::kCpl; ++c) {
             const int ci = lane_in_group + c * S::kLpt;
             uint4 raw = make_uint4(0, 0, 0, 0);
-            if (ci < S::kChunks) raw = *reinterpret_cast<const uint4*>(ktile + tt * D + ci * 8);
+            if (ci < S::kChunks && live[j]) raw = *reinterpret_cast<const uint4*>(ktile + tt * D + ci * 8);
             const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
@@ -236,17 +241,48 @@ __global__ void __launch_bounds__(DecodeShape<D>::kThreads, 1)
               kf[c * 8 + 2 * e + 1] = f.y;
             }
           }
-          float sc[kRows];
 #pragma unroll
           for (int r = 0; r < kRows; ++r) {
             float dot = 0.f;
+            if (r < nrows) {  // uniform: rows past the query length take no work
+              float part[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-            for (int e = 0; e < S::kCpl * 8; ++e) dot = fmaf(qv[r][e], kf[e], dot);
-            // Only this group's lanes take part: groups leave the token loop independently.
+              for (int e = 0; e < S::kCpl * 8; ++e) part[e % 4] = fmaf(qv[r][e], kf[e], part[e % 4]);
+              dot = (part[0] + part[1]) + (part[2] + part[3]);
+              // Only this group's lanes take part: groups leave the tile independently.
 #pragma unroll
-            for (int off = S::kLpt / 2; off > 0; off >>= 1) dot += __shfl_xor_sync(group_mask, dot, off);
-            sc[r] = dot;
+              for (int off = S::kLpt / 2; off > 0; off >>= 1) dot += __shfl_xor_sync(group_mask, dot, off);
+            }
+            sc[j][r] = dot;
           }
+        }
+        float pr[S::kTpg][kRows];
+#pragma unroll
+        for (int r = 0; r < kRows; ++r) {
+          float mt = m[r];
+#pragma unroll
+          for (int j = 0; j < S::kTpg; ++j) {
+            const bool use = live[j] && r < nrows && tok0 + group + j * S::kGroups < vis[r];
+            if (use) mt = fmaxf(mt, sc[j][r]);
+          }
+          if (mt > m[r]) {
+            const float corr = fast_exp2(m[r] - mt);  // exp2(-inf) = 0 on the first key
+            l[r] *= corr;
+#pragma unroll
+            for (int e = 0; e < S::kCpl * 8; ++e) acc[r][e] *= corr;
+            m[r] = mt;
+          }
+#pragma unroll
+          for (int j = 0; j < S::kTpg; ++j) {
+            const bool use = live[j] && r < nrows && tok0 + group + j * S::kGroups < vis[r];
+            pr[j][r] = use ? fast_exp2(sc[j][r] - m[r]) : 0.f;
+            l[r] += pr[j][r];
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < S::kTpg; ++j) {
+          if (!live[j]) continue;  // uniform within the group
+          const int tt = group + j * S::kGroups;
           float vf[S::kCpl * 8];
 #pragma unroll
           for (int c = 0; c < S::kCpl; ++c) {
@@ -263,18 +299,10 @@ __global__ void __launch_bounds__(DecodeShape<D>::kThreads, 1)
           }
 #pragma unroll
           for (int r = 0; r < kRows; ++r) {
-            if (tok < vis[r]) {
-              if (sc[r] > m[r]) {
-                const float corr = fast_exp2(m[r] - sc[r]);  // exp2(-inf) = 0 on the first key
-                l[r] *= corr;
+            // masked tokens (p = 0) stay out of the accumulator entirely: V rows past a cache's end may be NaN
+            if (pr[j][r] != 0.f) {
 #pragma unroll
-                for (int e = 0; e < S::kCpl * 8; ++e) acc[r][e] *= corr;
-                m[r] = sc[r];
-              }
-              const float pr = fast_exp2(sc[r] - m[r]);
-              l[r] += pr;
-#pragma unroll
-              for (int e = 0; e < S::kCpl * 8; ++e) acc[r][e] = fmaf(pr, vf[e], acc[r][e]);
+              for (int e = 0; e < S::kCpl * 8; ++e) acc[r][e] = fmaf(pr[j][r], vf[e], acc[r][e]);
             }
           }
         }
