@@ -630,11 +630,11 @@ __global__ void __launch_bounds__(384, 1)
         }
         if (row_valid && a.write_partials) a.part_lse[row_id * a.splits + c.s] = own_lse;
       } else {
-        // A piece of an item cut between programs. Pieces count themselves in (arrival counter per item)
-        // only after writing their partial to this program's slot (2 p for the piece a program starts with,
-        // 2 p + 1 for the one it ends with). The piece that finds every other piece already counted merges
-        // them with its own O straight from TMEM and writes nothing else; if two pieces race past that check,
-        // both write and the one whose count completes the set merges. No CTA ever waits for another.
+        // A piece of an item cut between programs. Every piece writes its partial (FP32 O and base-2 LSE) to
+        // its program's slot (2 p for the piece a program starts with, 2 p + 1 for the one it ends with), then
+        // counts itself in on the item's arrival counter; the piece whose count completes the set merges all
+        // pieces from their slots in piece order, so the result does not depend on which CTA finished last.
+        // No CTA ever waits for another.
         const long long total = a.prog_u[a.programs];
         const int q_first = program_of(total, a.programs, sg.item_u);
         const int pieces = program_of(total, a.programs, sg.item_u + sg.units - 1) - q_first + 1;
@@ -644,79 +644,56 @@ __global__ void __launch_bounds__(384, 1)
         auto piece_row = [&](int k) -> long long {
           return (2ll * q_first + first_extra + (k == 0 ? 0 : 2 * k - first_extra)) * kPairRows + 128 * t + row;
         };
-        if (warp == 4 && lane == 0) *merge_flag = ld_acquire_gpu(&a.counters[sg.item]) == pieces - 1 ? 1 : 0;
-        named_barrier_sync(1, 256);
-        int merge = *merge_flag;
-        named_barrier_sync(1, 256);  // read by all before the next write
-        if (!merge) {
-          const long long my_row = piece_row(own);
-          for (int cb = 0; cb < D / 16; ++cb) {
-            float o[16];
-            load_o(cb, o);  // warp-collective: every lane, valid row or not
-            if (row_valid) {
-              float4* dst = reinterpret_cast<float4*>(a.slot_o + my_row * D + cb * 16);
+        const long long my_row = piece_row(own);
+        for (int cb = 0; cb < D / 16; ++cb) {
+          float o[16];
+          load_o(cb, o);  // warp-collective: every lane, valid row or not
+          if (row_valid) {
+            float4* dst = reinterpret_cast<float4*>(a.slot_o + my_row * D + cb * 16);
 #pragma unroll
-              for (int i = 0; i < 4; ++i) dst[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
-            }
+            for (int i = 0; i < 4; ++i) dst[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
           }
-          if (row_valid) a.slot_lse[my_row] = own_lse;
-          named_barrier_sync(1, 256);  // both warpgroups have written their rows
-          if (warp == 4 && lane == 0) {
-            __threadfence();
-            *merge_flag = atomicAdd(&a.counters[sg.item], 1) + 1 == pieces ? 1 : 0;
-          }
-          named_barrier_sync(1, 256);
-          merge = *merge_flag;
-          named_barrier_sync(1, 256);
         }
+        if (row_valid) a.slot_lse[my_row] = own_lse;
+        named_barrier_sync(1, 256);  // both warpgroups have written their rows
+        if (warp == 4 && lane == 0) {
+          __threadfence();
+          *merge_flag = atomicAdd(&a.counters[sg.item], 1) + 1 == pieces ? 1 : 0;
+        }
+        named_barrier_sync(1, 256);
+        const int merge = *merge_flag;
+        named_barrier_sync(1, 256);  // read by all before the next write
         if (merge) {
           __threadfence();
           if (warp == 4 && lane == 0) a.counters[sg.item] = 0;  // ready for the next launch
-          // base-2 LSE merge (the split merge's arithmetic, merge_kernel in fgw_aux.cu); own piece from TMEM.
-          // The pieces are combined in piece order whichever of them merges (its own normalised O and LSE are
-          // the values it would have written to its slot), so the result does not depend on which CTA
-          // finished last. Every lane runs the TMEM loads (warp-collective); only valid rows touch global memory.
-          float peak = own_lse;
-          float wsum = 0.f;
+          // base-2 LSE merge (the split merge's arithmetic, merge_kernel in fgw_aux.cu)
           if (row_valid) {
+            float peak = kEmptyLse;
+            for (int k = 0; k < pieces; ++k) peak = fmaxf(peak, __ldcg(&a.slot_lse[piece_row(k)]));
+            float wsum = 0.f;
             for (int k = 0; k < pieces; ++k) {
-              if (k != own) peak = fmaxf(peak, __ldcg(&a.slot_lse[piece_row(k)]));
-            }
-            for (int k = 0; k < pieces; ++k) {
-              const float lse = k == own ? own_lse : __ldcg(&a.slot_lse[piece_row(k)]);
+              const float lse = __ldcg(&a.slot_lse[piece_row(k)]);
               if (lse > kValidLse) wsum += fast_exp2(lse - peak);
             }
-          }
-          const float scale = wsum > 0.f ? 1.f / wsum : 0.f;
-          for (int cb = 0; cb < D / 16; ++cb) {
-            float mine[16];
-            load_o(cb, mine);  // warp-collective: every lane, valid row or not
-            if (row_valid) {
+            const float scale = wsum > 0.f ? 1.f / wsum : 0.f;
+            for (int cb = 0; cb < D / 16; ++cb) {
               float acc[16];
 #pragma unroll
               for (int i = 0; i < 16; ++i) acc[i] = 0.f;
               for (int k = 0; k < pieces; ++k) {
                 const long long pr = piece_row(k);
-                const float lse = k == own ? own_lse : __ldcg(&a.slot_lse[pr]);
+                const float lse = __ldcg(&a.slot_lse[pr]);
                 if (!(lse > kValidLse)) continue;
                 const float w = fast_exp2(lse - peak);
-                float v[16];
-                if (k == own) {
+                const float4* src = reinterpret_cast<const float4*>(a.slot_o + pr * D + cb * 16);
 #pragma unroll
-                  for (int i = 0; i < 16; ++i) v[i] = mine[i];
-                } else {
-                  const float4* src = reinterpret_cast<const float4*>(a.slot_o + pr * D + cb * 16);
-#pragma unroll
-                  for (int i = 0; i < 4; ++i) {
-                    const float4 x = __ldcg(src + i);
-                    v[4 * i] = x.x;
-                    v[4 * i + 1] = x.y;
-                    v[4 * i + 2] = x.z;
-                    v[4 * i + 3] = x.w;
-                  }
+                for (int i = 0; i < 4; ++i) {
+                  const float4 v = __ldcg(src + i);
+                  acc[4 * i] += w * v.x;
+                  acc[4 * i + 1] += w * v.y;
+                  acc[4 * i + 2] += w * v.z;
+                  acc[4 * i + 3] += w * v.w;
                 }
-#pragma unroll
-                for (int i = 0; i < 16; ++i) acc[i] = fmaf(w, v[i], acc[i]);
               }
               store_row(cb, acc, scale);
             }
