@@ -30,6 +30,7 @@ PATH_TENSOR = 2
 SCHEDULE_AUTO = 0
 SCHEDULE_STRIDED = 1
 SCHEDULE_CONTIGUOUS = 2
+SCHEDULE_TAIL = 3
 
 ABI_VERSION = 3  # FGW_MHA_ABI_VERSION the Params / GatherParams layouts below match
 

@@ -51,7 +51,8 @@ bool use_stream_schedule(const fgw_mha_params& p) {
   const bool applies = resolve_path(p) == FGW_PATH_TENSOR && p.head_dim <= 128 && p.num_splits == 1 &&
                        !single_tile_requested() && pair_items(p) <= kStreamMaxItems;
   if (!applies) return false;
-  return p.schedule == FGW_SCHEDULE_CONTIGUOUS || 3 * pair_items(p) < 2ll * kStreamMaxPrograms;
+  return p.schedule == FGW_SCHEDULE_CONTIGUOUS || p.schedule == FGW_SCHEDULE_TAIL ||
+         3 * pair_items(p) < 2ll * kStreamMaxPrograms;
 }
 
 namespace {
@@ -148,7 +149,7 @@ static int validate(const fgw_mha_params* p) {
   if (p->num_splits < 1 || p->num_splits > 1024) return FGW_ERR_INVALID_ARGUMENT;
   if (p->grid_cap < 0 || p->wait_budget_ms < 0) return FGW_ERR_INVALID_ARGUMENT;
   if (p->path < FGW_PATH_AUTO || p->path > FGW_PATH_TENSOR) return FGW_ERR_INVALID_ARGUMENT;
-  if (p->schedule < FGW_SCHEDULE_AUTO || p->schedule > FGW_SCHEDULE_CONTIGUOUS) return FGW_ERR_INVALID_ARGUMENT;
+  if (p->schedule < FGW_SCHEDULE_AUTO || p->schedule > FGW_SCHEDULE_TAIL) return FGW_ERR_INVALID_ARGUMENT;
   for (int i = 0; i < 3; ++i) {
     if (p->reserved[i] != 0) return FGW_ERR_INVALID_ARGUMENT;
   }
@@ -199,6 +200,8 @@ static int prepare(const fgw_mha_params* params, void* workspace, size_t workspa
   if (d.contiguous) {
     const int cap = d.p.grid_cap > 0 ? d.p.grid_cap : d.sm_count;
     d.programs = std::min(std::min(cap, d.sm_count), kStreamMaxPrograms);
+    // TAIL: whole items for the full waves, cut only the last partial wave's items
+    d.tail_start = d.p.schedule == FGW_SCHEDULE_TAIL ? (d.items / d.programs) * d.programs : 0;
   }
   return FGW_OK;
 }

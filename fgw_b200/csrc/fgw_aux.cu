@@ -18,10 +18,12 @@ namespace fgw {
 constexpr int kPlanSortMax = 8192;
 
 // Contiguous schedule, planned on the device from the clamped lengths: the work items of the two-tile
-// kernel in its item order, each counting max(KV tiles, 1) units; program p gets units
-// [p * (total / G) + min(p, total % G), ...) as in the reference's balanced plan (static_schedule.py:64-66).
+// kernel in its item order (under the tail schedule only those of the last, partial wave), each counting
+// max(KV tiles, 1) units; program p gets units [p * (total / G) + min(p, total % G), ...) as in the
+// reference's balanced plan (static_schedule.py:64-66).
 struct StreamPlanArgs {
   int enabled, items, programs, heads, sq, causal, qpairs;
+  int first;  // first item of the cut range (0, or the items of the full waves under the tail schedule)
   int32_t* prog_item;
   int32_t* prog_off;
   long long* prog_u;
@@ -92,14 +94,16 @@ __global__ void __launch_bounds__(1024) plan_kernel(const int32_t* __restrict__ 
   }
   if (!sp.enabled) return;
   __syncthreads();  // lens and order are read below by other threads of this block
-  // exclusive prefix of item units: each thread sums a contiguous chunk, the chunk sums are scanned
-  const int per = (sp.items + blockDim.x - 1) / blockDim.x;
-  const int lo = min(sp.items, static_cast<int>(threadIdx.x) * per);
-  const int hi = min(sp.items, lo + per);
+  // exclusive prefix of the units of items [first, items) (indices relative to `first`): each thread sums a
+  // contiguous chunk, the chunk sums are scanned
+  const int n = sp.items - sp.first;
+  const int per = (n + blockDim.x - 1) / blockDim.x;
+  const int lo = min(n, static_cast<int>(threadIdx.x) * per);
+  const int hi = min(n, lo + per);
   long long local = 0;
   for (int i = lo; i < hi; ++i) {
-    local += stream_item_units(sp, lens, order, i);
-    sp.counters[i] = 0;
+    local += stream_item_units(sp, lens, order, sp.first + i);
+    sp.counters[sp.first + i] = 0;
   }
   chunk_sum[threadIdx.x] = local;
   __syncthreads();
@@ -110,22 +114,22 @@ __global__ void __launch_bounds__(1024) plan_kernel(const int32_t* __restrict__ 
       chunk_sum[t] = run;
       run += v;
     }
-    sp.prefix[sp.items] = run;
+    sp.prefix[n] = run;
   }
   __syncthreads();
   long long run = chunk_sum[threadIdx.x];
   for (int i = lo; i < hi; ++i) {
     sp.prefix[i] = run;
-    run += stream_item_units(sp, lens, order, i);
+    run += stream_item_units(sp, lens, order, sp.first + i);
   }
   __syncthreads();
   // program starts: the item holding unit U_p (the last item whose first unit is <= U_p)
-  const long long total = sp.prefix[sp.items];
+  const long long total = sp.prefix[n];
   for (int p = threadIdx.x; p <= sp.programs; p += blockDim.x) {
     const long long u = stream_program_start(total, sp.programs, p);
     sp.prog_u[p] = u;
     if (p == sp.programs) continue;
-    int a = 0, b = sp.items;  // prefix[a] <= u < prefix[b] (b == items when u == total)
+    int a = 0, b = n;  // prefix[a] <= u < prefix[b] (b == n when u == total)
     while (b - a > 1) {
       const int mid = (a + b) / 2;
       if (sp.prefix[mid] <= u) {
@@ -138,7 +142,7 @@ __global__ void __launch_bounds__(1024) plan_kernel(const int32_t* __restrict__ 
       sp.prog_item[p] = sp.items;
       sp.prog_off[p] = 0;
     } else {
-      sp.prog_item[p] = a;
+      sp.prog_item[p] = sp.first + a;
       sp.prog_off[p] = static_cast<int32_t>(u - sp.prefix[a]);
     }
   }
@@ -157,6 +161,7 @@ cudaError_t launch_plan(const LaunchDesc& d) {
   if (d.contiguous) {
     sp.enabled = 1;
     sp.items = d.items;
+    sp.first = d.tail_start;
     sp.programs = d.programs;
     sp.heads = d.p.heads;
     sp.sq = d.p.q_len;

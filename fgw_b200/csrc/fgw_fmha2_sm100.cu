@@ -34,6 +34,7 @@ struct Fmha2Args {
   // contiguous schedule (see fgw_schedule): per-program start item / unit offset / first unit, the
   // per-item arrival counters and the two partial slots of every program
   int contiguous, programs;
+  int tail_start;  // items below it are whole items of the full waves, dealt strided (tail schedule)
   const int32_t* prog_item;
   const int32_t* prog_off;
   const long long* prog_u;
@@ -134,36 +135,40 @@ struct Segment {
 };
 
 struct SegmentCursor {
+  long long whole;  // next whole item (strided part)
   long long item;
   int off;
   long long u, u_end;
 };
 
 __device__ __forceinline__ void cursor_init(const Fmha2Args& a, SegmentCursor& k) {
+  k.whole = blockIdx.x;
   if (a.contiguous) {
     k.item = a.prog_item[blockIdx.x];
     k.off = a.prog_off[blockIdx.x];
     k.u = a.prog_u[blockIdx.x];
     k.u_end = a.prog_u[blockIdx.x + 1];
   } else {
-    k.item = blockIdx.x;
+    k.item = 0;
     k.off = 0;
     k.u = k.u_end = 0;
   }
 }
 
-// Every role of the CTA walks the same segments in the same order.
+// Every role of the CTA walks the same segments in the same order: whole items first (all of them with the
+// strided schedule, those of the full waves with the tail schedule), then its contiguous range of units.
 __device__ __forceinline__ bool next_segment(const Fmha2Args& a, SegmentCursor& k, Segment& sg) {
-  if (!a.contiguous) {
-    if (k.item >= a.items) return false;
-    sg.item = static_cast<int>(k.item);
-    pair_item(a, k.item, sg.c);
+  const long long whole_end = a.contiguous ? a.tail_start : a.items;
+  if (k.whole < whole_end) {
+    sg.item = static_cast<int>(k.whole);
+    pair_item(a, k.whole, sg.c);
     sg.piece = false;
     sg.item_u = sg.u0 = 0;
     sg.units = 0;
-    k.item += gridDim.x;
+    k.whole += gridDim.x;
     return true;
   }
+  if (!a.contiguous) return false;
   if (k.u >= k.u_end) return false;
   sg.item = static_cast<int>(k.item);
   pair_item(a, k.item, sg.c);  // one split: the whole item
@@ -766,6 +771,7 @@ cudaError_t launch_tensor_pairs(const LaunchDesc& d, bool write_partials, const 
   args.budget_ns = d.budget_ns;
   args.contiguous = d.contiguous ? 1 : 0;
   args.programs = d.contiguous ? d.programs : 0;
+  args.tail_start = d.contiguous ? d.tail_start : 0;
   args.prog_item = d.prog_item;
   args.prog_off = d.prog_off;
   args.prog_u = d.prog_u;

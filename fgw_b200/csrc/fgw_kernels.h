@@ -32,6 +32,7 @@ struct LaunchDesc {
   bool contiguous;
   int programs;
   int items;
+  int tail_start;      // first item of the cut range: 0 (CONTIGUOUS) or the items of the full waves (TAIL)
   int32_t* prog_item;  // [programs]
   int32_t* prog_off;   // [programs]
   long long* prog_u;   // [programs + 1]

@@ -110,8 +110,8 @@ def build_kernel(batch, sq, heads, dim, pool_rows, width, page_size, causal, dty
         raise ValueError("positive page size, whole pool pages and positive table width required")
     if page_size % 16:
         raise ValueError("page_size must be a multiple of 16")
-    if task_assignment not in (None, "strided", "contiguous"):
-        raise ValueError("task_assignment must be None (route default), strided or contiguous")
+    if task_assignment not in (None, "strided", "contiguous", "tail"):
+        raise ValueError("task_assignment must be None (route default), strided, contiguous or tail")
     if schedule_mode not in ("auto", "auto-offset", "manual", "nsa"):
         raise ValueError("schedule_mode must be auto, auto-offset, manual or nsa")
     if split_policy not in ("auto", "legacy", "cost_model"):
@@ -215,7 +215,7 @@ def build_kernel(batch, sq, heads, dim, pool_rows, width, page_size, causal, dty
     params.grid_cap = grid_cap
     params.path = kernel_path
     params.schedule = {None: _native.SCHEDULE_AUTO, "strided": _native.SCHEDULE_STRIDED,
-                       "contiguous": _native.SCHEDULE_CONTIGUOUS}[task_assignment]
+                       "contiguous": _native.SCHEDULE_CONTIGUOUS, "tail": _native.SCHEDULE_TAIL}[task_assignment]
     workspace_bytes = _native.workspace_size(params)
     # The contiguous schedule applies to the two-tile tensor kernel with one split (fgw_schedule in
     # include/fgw_mha.h); elsewhere the work items are dealt out strided in longest-request-first order.
@@ -223,7 +223,7 @@ def build_kernel(batch, sq, heads, dim, pool_rows, width, page_size, causal, dty
     contiguous = (kernel_path == _native.PATH_TENSOR and dim <= 128 and splits == 1
                   and task_assignment != "strided" and pair_items <= 65536
                   and os.environ.get("FGW_MHA_TENSOR_SINGLE_TILE") != "1"
-                  and (task_assignment == "contiguous" or 3 * pair_items < 2 * 148))
+                  and (task_assignment in ("contiguous", "tail") or 3 * pair_items < 2 * 148))
 
     def _bind(q, k, v, table, lengths, out):
         p = _native.Params.from_buffer_copy(params)
@@ -265,7 +265,8 @@ def build_kernel(batch, sq, heads, dim, pool_rows, width, page_size, causal, dty
 
     launch.block_q = block_q
     launch.compute_grid = compute_grid
-    launch.task_assignment = "contiguous" if contiguous else "strided"
+    launch.task_assignment = (task_assignment if task_assignment == "tail" else "contiguous") if contiguous \
+        else "strided"
     if contiguous:
         compute_grid = min(cores, 148) if grid_cap == 0 else min(grid_cap, cores, 148)
         launch.compute_grid = compute_grid

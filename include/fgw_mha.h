@@ -75,13 +75,18 @@ typedef enum fgw_path {
  *               of equal length (loads differ by at most one tile); an item cut between CTAs is computed in
  *               pieces whose partial results the CTA finishing last merges in the same launch. Tensor path
  *               with num_splits == 1 and head_dim <= 128 only.
+ *   TAIL:       STRIDED for the full waves (the first floor(items / G) * G items, G = the programs), then
+ *               CONTIGUOUS over the items of the last, partial wave only (the reference's tail plan,
+ *               static_schedule.py:83-116 `make_tail_plan`): only those items are cut into pieces. Same
+ *               restrictions as CONTIGUOUS.
  *   AUTO:       CONTIGUOUS where it applies and there are fewer work items than 2/3 of 148 programs (whole
  *               items would leave SMs idle), STRIDED otherwise.
  */
 typedef enum fgw_schedule {
   FGW_SCHEDULE_AUTO = 0,
   FGW_SCHEDULE_STRIDED = 1,
-  FGW_SCHEDULE_CONTIGUOUS = 2
+  FGW_SCHEDULE_CONTIGUOUS = 2,
+  FGW_SCHEDULE_TAIL = 3
 } fgw_schedule;
 
 /*

@@ -56,7 +56,7 @@ def test_schedule_is_validated_and_sizes_the_workspace():
     assert (_native.workspace_size(_params(**many))
             == _native.workspace_size(_params(schedule=_native.SCHEDULE_STRIDED, **many)))
     with pytest.raises(_native.FgwError):
-        _native.check(_native.library().fgw_mha_paged_fwd(ctypes.byref(_params(schedule=3)), None, 0, None),
+        _native.check(_native.library().fgw_mha_paged_fwd(ctypes.byref(_params(schedule=4)), None, 0, None),
                       "fgw_mha_paged_fwd")
     # splits > 1 or the decode path keep the strided layout
     assert (_native.workspace_size(_params(q_len=4096, num_splits=2, path=_native.PATH_TENSOR))
