@@ -318,6 +318,13 @@ def run_longq(args, rank, world, device, stream):
         barrier(world)
     step_ms = sum(graph_totals) / len(graph_totals)
 
+    # The reference's own protocol (bench_mha_mfu.py:221-247): median of 51 CUDA-event samples after 20
+    # warm-ups, with a warm L2 and with the L2 flushed before every sample. Outside the K timed steps above.
+    protocol = {}
+    for name, fl in (("warm_l2", None), ("flushed_l2", flush)):
+        _, samples = timed_steps([("step", graph.replay)], 51, 20, fl, stream)
+        protocol[name + "_us_median"] = statistics.median(samples) * 1e3
+
     # End to end through the public API: pinned host inputs -> device -> forward -> host output.
     host = {k: inp[k].cpu().pin_memory() for k in ("q", "k", "v", "table", "lengths")}
     dev_bufs = {k: torch.empty_like(inp[k]) for k in host}
@@ -339,7 +346,7 @@ def run_longq(args, rank, world, device, stream):
     ok = check_longq(inp, out)
     del graph
     return {"kernel": kernel, "inp": inp, "flops": flops, "step_ms": step_ms, "attend_ms": attend_ms,
-            "eager_step_ms": eager_step_ms,
+            "eager_step_ms": eager_step_ms, "protocol": protocol,
             "per": per, "e2e_ms": e2e_ms, "h2d": h2d, "d2h": d2h, "clocks": clocks.summary(), "parity": ok,
             "launches_per_step": len(fns)}
 
@@ -673,6 +680,11 @@ def main(argv=None):
             "gpu_launches": lq["launches_per_step"] * args.steps,
             "stage_ms": {n: statistics.mean(v) for n, v in lq["per"].items()},
             "eager_step_ms": max_over_ranks(lq["eager_step_ms"], world),
+            "reference_protocol": {
+                "what": "median of 51 CUDA-graph steps after 20 warm-ups (FGW bench_mha_mfu.py), max over ranks",
+                **{k: max_over_ranks(v / 1e3, world) * 1e3 for k, v in lq["protocol"].items()},
+                "warm_l2_tflops": total_flops / (max_over_ranks(lq["protocol"]["warm_l2_us_median"] / 1e3, world)
+                                                 * 1e-3) / 1e12},
             "step_timing": "CUDA-graph replay of plan+attend(+merge), L2 flushed before each step; stage_ms and "
                            "roofline from per-launch events of the same step run eagerly",
         })
