@@ -41,9 +41,11 @@ struct DecodeShape {
   static constexpr int kLpt = kChunks >= 8 ? 8 : (kChunks >= 4 ? 4 : 2);  // lanes per token
   static constexpr int kCpl = (kChunks + kLpt - 1) / kLpt;  // chunks per lane
   static constexpr int kGpw = 32 / kLpt;                   // token groups per warp
-  static constexpr int kWarps = 8;                         // consumer warps
+  // consumer warps: the consumers are latency-bound, so small rows get 12 (the register budget of 416
+  // threads still covers them); 8 above D = 128
+  static constexpr int kWarps = D <= 128 ? 12 : 8;
   static constexpr int kGroups = kWarps * kGpw;
-  static constexpr int kTile = kGroups > 64 ? kGroups : 64;  // tokens per pipeline stage
+  static constexpr int kTile = kGroups * ((64 + kGroups - 1) / kGroups);  // tokens per stage: >= 64, whole groups
   static constexpr int kTpg = kTile / kGroups;             // tokens per group per tile
   static constexpr int kRows = (kCpl * 8 >= 32) ? 1 : ((kCpl * 8 >= 16) ? 2 : 4);  // query rows per item
   static constexpr int kThreads = (kWarps + 1) * 32;
@@ -53,7 +55,7 @@ template <typename T, int D>
 struct DecodeSmem {
   using S = DecodeShape<D>;
   static constexpr int kStageBytes = 2 * S::kTile * D * (int)sizeof(T);
-  static constexpr int kStages = std::min(8, std::max(2, (160 * 1024) / kStageBytes));
+  static constexpr int kStages = std::min(8, std::max(2, (192 * 1024) / kStageBytes));
   static constexpr int kRedFloats = S::kWarps * S::kRows * (D + 2);
   static constexpr int kBytes = kStages * kStageBytes + 2 * kStages * 8 + kRedFloats * 4 + 64;
 };
@@ -398,6 +400,34 @@ static cudaError_t launch_decode_t(const LaunchDesc& d, const DecodeArgs& args, 
   return cudaGetLastError();
 }
 
+// Tokens per pipeline stage of the decode kernel for this head dimension (the TMA box rows must divide it).
+static int decode_tile_tokens(int head_dim) {
+  switch (head_dim) {
+#define FGW_TILE_CASE(DD) \
+  case DD:                \
+    return DecodeShape<DD>::kTile;
+    FGW_TILE_CASE(16)
+    FGW_TILE_CASE(32)
+    FGW_TILE_CASE(48)
+    FGW_TILE_CASE(64)
+    FGW_TILE_CASE(80)
+    FGW_TILE_CASE(96)
+    FGW_TILE_CASE(112)
+    FGW_TILE_CASE(128)
+    FGW_TILE_CASE(144)
+    FGW_TILE_CASE(160)
+    FGW_TILE_CASE(176)
+    FGW_TILE_CASE(192)
+    FGW_TILE_CASE(208)
+    FGW_TILE_CASE(224)
+    FGW_TILE_CASE(240)
+    FGW_TILE_CASE(256)
+#undef FGW_TILE_CASE
+    default:
+      return 64;
+  }
+}
+
 int decode_rows_per_item(int head_dim) {
   switch (head_dim) {
 #define FGW_ROWS_CASE(DD) \
@@ -467,7 +497,7 @@ cudaError_t launch_decode(const LaunchDesc& d, bool write_partials) {
   args.splits = p.num_splits;
   args.causal = p.causal;
   args.row_blocks = (p.q_len + rows - 1) / rows;
-  args.box_rows = gcd_int(p.page_size, 64);
+  args.box_rows = gcd_int(gcd_int(p.page_size, decode_tile_tokens(p.head_dim)), 256);  // divides page and tile
   args.write_partials = write_partials ? 1 : 0;
   args.items = (long long)p.batch * args.row_blocks * p.num_splits * p.heads;
   args.scale_log2 = (1.0f / sqrtf((float)p.head_dim)) * kLog2e;
