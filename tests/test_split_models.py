@@ -117,3 +117,16 @@ def test_b200_model_selection_on_the_sweep():
             if str(pick) in r["median_us"]:
                 regret.append(r["median_us"][str(pick)] / min(r["median_us"].values()))
     assert len(regret) > 40 and max(regret) < 1.5
+
+
+def test_work_accounting_matches_the_oracle():
+    # the product's FLOP/byte accounting (reported by bench.py) equals the oracle's restatement of FGW's policy
+    import oracle
+    from fgw_b200.operators.mha import work
+    for lengths in ([2048, 2048], [0, 1, 130, 4096], [17, 0], [32768]):
+        for sq in (1, 8, 129, 4096):
+            for causal in (False, True):
+                assert work.useful_flops(lengths, sq, 8, 128, causal) == oracle.useful_flops(lengths, sq, 8, 128, causal)
+        assert (work.algorithmic_bytes(lengths, len(lengths), 4, 8, 128, 16, 2)
+                == oracle.algorithmic_bytes(lengths, len(lengths), 4, 8, 128, 16, 2))
+    assert work.useful_flops([2048, 2048], 4096, 8, 128, False) == 68_719_476_736  # config 2: 68.72 GFLOP
