@@ -137,13 +137,6 @@ __device__ __forceinline__ bool mbar_wait_all(uint64_t* b0, uint32_t p0, uint64_
   }
 }
 
-// Acquire load of a global word at GPU scope (a flag or counter written by other CTAs).
-__device__ __forceinline__ int ld_acquire_gpu(const int32_t* p) {
-  int v;
-  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
 // Named barrier over a subset of warps (id 0 is __syncthreads).
 __device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
@@ -304,20 +297,10 @@ __device__ __forceinline__ void umma_f16_ss(uint32_t d_tmem, uint64_t a_desc, ui
       : "memory");
 }
 
-// D[tmem] (+)= A[tmem] * B[smem desc]: A (M x K, K-major) read from tensor memory, one row per lane,
-// two 16-bit elements per 32-bit column (element 2c in the low half of column c).
-__device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
-                                            uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-// The same two UMMA forms with each shared-memory descriptor passed as its two 32-bit words (see
-// umma_desc_lo / umma_desc_hi), so an issue loop only adds an offset to the low word per instruction.
+// UMMA issue with each shared-memory descriptor passed as its two 32-bit words (see umma_desc_lo /
+// umma_desc_hi), so an issue loop only adds an offset to the low word per instruction. umma_f16_ss_w reads A
+// from shared memory; umma_f16_ts_w reads A (M x K, K-major) from tensor memory, one row per lane, two 16-bit
+// elements per 32-bit column (element 2c in the low half of column c).
 __device__ __forceinline__ void umma_f16_ss_w(uint32_t d_tmem, uint32_t a_lo, uint32_t a_hi, uint32_t b_lo,
                                               uint32_t b_hi, uint32_t idesc, uint32_t accumulate) {
   asm volatile(

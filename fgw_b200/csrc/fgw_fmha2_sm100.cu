@@ -206,12 +206,6 @@ __device__ __forceinline__ int program_of(long long total, int programs, long lo
   return static_cast<int>(r + (u - r * (b + 1)) / b);
 }
 
-// Partial slot of item piece held by program q: slot 2q for the program's first segment, 2q + 1 for its
-// last (a program holds at most two pieces: one it starts with, one it ends with).
-__device__ __forceinline__ int piece_slot(long long total, int programs, int q, int q_first, long long item_u) {
-  return 2 * q + ((q == q_first && item_u != program_start(total, programs, q)) ? 1 : 0);
-}
-
 template <typename T, int NB>
 __global__ void __launch_bounds__(384, 1)
     fmha2_sm100_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
