@@ -57,8 +57,9 @@ extern "C" int fgw_mha_paged_fwd_static_ws(const fgw_mha_params* params, void* s
   void* ws = nullptr;
   st = static_workspace_ptr(&ws);
   if (st != FGW_OK) return st;
-  // The plan kernel that starts every forward clears the error word; every other byte of scratch the
-  // kernels read (lengths, order, partials) is written earlier in the same call, so the previous
-  // call's leftovers never reach an output.
+  // What must start at zero is zeroed on the device by the plan kernel that starts every forward: the
+  // error word and the per-item arrival counters the contiguous and tail schedules' piece merges count
+  // on. Every other byte of scratch the kernels read (lengths, order, partials) is written earlier in
+  // the same call, so the previous call's leftovers never reach an output.
   return fgw_mha_paged_fwd(&p, ws, FGW_MHA_STATIC_WORKSPACE_BYTES, stream);
 }

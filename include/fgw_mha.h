@@ -167,12 +167,16 @@ FGW_API int fgw_mha_merge(const fgw_mha_params* params, void* workspace, size_t 
 /* Allocation-free forward, for callers that cannot allocate device memory where they run attention
  * (inside an allocator or memory-pool callback, in a serving loop that forbids allocator calls, or in a
  * plugin whose host owns all device memory). No counterpart in the reference, which allocates its
- * scratch per call. Same kernels and results as fgw_mha_paged_fwd, but the workspace is a file-scope
- * device array of FGW_MHA_STATIC_WORKSPACE_BYTES held by every GPU that loads the library until exit;
- * nothing is allocated or freed. Returns FGW_ERR_WORKSPACE_TOO_SMALL when fgw_mha_workspace_size(params)
- * exceeds that size. The first call on a device looks up the array's device address on the current
- * device; make that first call before any stream capture. All calls share the one array, so calls that
- * overlap on the GPU (different streams, or threads) race: serialise them. */
+ * scratch per call. Same kernels as fgw_mha_paged_fwd, but the workspace is a file-scope device array
+ * of FGW_MHA_STATIC_WORKSPACE_BYTES held by every GPU that loads the library until exit; nothing is
+ * allocated or freed. When an FGW_SCHEDULE_AUTO request's contiguous-schedule partial slots would not
+ * fit, it runs the strided schedule instead (results then agree with fgw_mha_paged_fwd within the
+ * library's floating-point tolerance, not bit for bit). Returns FGW_ERR_WORKSPACE_TOO_SMALL when the
+ * request still needs more than that size. Counters and the error word that must start at zero are
+ * zeroed on the device by each call's first kernel. The first call on a device looks up the array's
+ * device address on the current device; make that first call before any stream capture. All calls
+ * share the one array, so calls that overlap on the GPU (different streams, or threads) race:
+ * serialise them. */
 FGW_API int fgw_mha_paged_fwd_static_ws(const fgw_mha_params* params, void* stream);
 
 /* Synchronises `stream`, then reports the device-side status recorded in the workspace header
