@@ -22,15 +22,18 @@ def _params_for(kernel, args, out):
     return p
 
 
-# (case, path, splits): split-KV cases so the scratch holds partials as well as the plan.
+# (case, path, splits, falls back): split-KV cases so the scratch holds partials as well as the plan, and
+# a one-split tensor case whose AUTO schedule is the contiguous one: its partial slots (2 x 148 x 256 x D
+# FP32) do not fit the array, so the entry point runs it on the strided schedule.
 CASES = [
-    (("nz_decode", 4, 1, 2, 128, 64, 8), "decode", 4),
-    (("nz_tensor", 2, 160, 2, 64, 16, 12), "tensor", 2),
+    (("nz_decode", 4, 1, 2, 128, 64, 8), "decode", 4, False),
+    (("nz_tensor", 2, 160, 2, 64, 16, 12), "tensor", 2, False),
+    (("nz_tensor_one_split", 2, 160, 2, 64, 16, 12), "tensor", 1, True),
 ]
 
 
-@pytest.mark.parametrize("case,path,splits", CASES, ids=[c[0][0] for c in CASES])
-def test_static_workspace_matches_regular_entry_point_twice(case, path, splits):
+@pytest.mark.parametrize("case,path,splits,falls_back", CASES, ids=[c[0][0] for c in CASES])
+def test_static_workspace_matches_regular_entry_point_twice(case, path, splits, falls_back):
     from fgw_b200 import _native
     from fgw_b200.operators.mha.current import build_kernel
     dev = torch.device("cuda", 0)
@@ -40,7 +43,10 @@ def test_static_workspace_matches_regular_entry_point_twice(case, path, splits):
         args = [inputs[key].to(dev) for key in ("q", "k", "v", "table", "lengths")]
         kernel = build_kernel(case[1], case[2], case[3], case[4], args[1].shape[0], case[6], case[5], causal,
                               "bfloat16", 0, cube_mode="general", num_splits=splits, path=path)
-        assert kernel.workspace_bytes <= _native.STATIC_WORKSPACE_BYTES
+        assert (kernel.workspace_bytes > _native.STATIC_WORKSPACE_BYTES) == falls_back
+        strided = _native.Params.from_buffer_copy(kernel.params)
+        strided.schedule = _native.SCHEDULE_STRIDED
+        assert _native.workspace_size(strided) <= _native.STATIC_WORKSPACE_BYTES
         expected = kernel(*args)
         got = torch.full_like(expected, float("nan"))
         _native.paged_fwd_static_ws(_params_for(kernel, args, got), stream)
