@@ -77,7 +77,12 @@ StreamSizes stream_sizes(const fgw_mha_params& p) {
 }
 }  // namespace
 
-size_t workspace_bytes(const fgw_mha_params& p, int /*path*/) {
+// Split-KV on the decode path keeps one arrival counter per output row group (fused merge).
+static bool decode_merge_counters(const fgw_mha_params& p, int path) {
+  return p.num_splits > 1 && path == FGW_PATH_DECODE;
+}
+
+size_t workspace_bytes(const fgw_mha_params& p, int path) {
   size_t bytes = sizeof(WorkspaceHeader);
   bytes += align256(sizeof(int32_t) * p.batch);  // lens
   bytes += align256(sizeof(int32_t) * p.batch);  // order
@@ -87,10 +92,11 @@ size_t workspace_bytes(const fgw_mha_params& p, int /*path*/) {
     bytes += align256(rows * p.num_splits * p.head_dim * sizeof(float));
   }
   if (use_stream_schedule(p)) bytes += stream_sizes(p).total();
+  if (decode_merge_counters(p, path)) bytes += align256(rows * sizeof(int32_t));
   return bytes;
 }
 
-void carve_workspace(LaunchDesc& d, void* workspace, int /*path*/) {
+void carve_workspace(LaunchDesc& d, void* workspace, int path) {
   const fgw_mha_params& p = d.p;
   uint8_t* base = static_cast<uint8_t*>(workspace);
   d.header = reinterpret_cast<WorkspaceHeader*>(base);
@@ -124,6 +130,11 @@ void carve_workspace(LaunchDesc& d, void* workspace, int /*path*/) {
     d.slot_lse = reinterpret_cast<float*>(base);
     base += z.slot_lse;
     d.slot_o = reinterpret_cast<float*>(base);
+    base += z.slot_o;
+  }
+  if (decode_merge_counters(p, path)) {
+    d.merge_counters = reinterpret_cast<int32_t*>(base);
+    d.merge_groups = static_cast<int>(rows);
   }
 }
 
@@ -206,9 +217,10 @@ static int prepare(const fgw_mha_params* params, void* workspace, size_t workspa
   return FGW_OK;
 }
 
-static int launch_main(const LaunchDesc& d, bool partials) {
+static int launch_main(const LaunchDesc& d, bool partials, bool fused_merge = false) {
   const int path = resolve_path(d.p);
-  cudaError_t err = path == FGW_PATH_TENSOR ? launch_tensor(d, partials) : launch_decode(d, partials);
+  cudaError_t err =
+      path == FGW_PATH_TENSOR ? launch_tensor(d, partials) : launch_decode(d, partials, partials && fused_merge);
   if (err == cudaErrorNotSupported) return FGW_ERR_UNSUPPORTED;
   return err == cudaSuccess ? FGW_OK : FGW_ERR_CUDA;
 }
@@ -269,9 +281,11 @@ int fgw_mha_paged_fwd(const fgw_mha_params* params, void* workspace, size_t work
   if (st != FGW_OK) return st;
   if (launch_plan(d) != cudaSuccess) return FGW_ERR_CUDA;
   const bool split = d.p.num_splits > 1;
-  st = launch_main(d, split);
+  // split-KV on the decode path merges in place (the CTA completing a row group's splits), no merge launch
+  const bool fused = d.merge_counters != nullptr;
+  st = launch_main(d, split, fused);
   if (st != FGW_OK) return st;
-  if (split && launch_merge(d) != cudaSuccess) return FGW_ERR_CUDA;
+  if (split && !fused && launch_merge(d) != cudaSuccess) return FGW_ERR_CUDA;
   return FGW_OK;
 }
 

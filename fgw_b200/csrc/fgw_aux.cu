@@ -9,7 +9,9 @@
 //   them into one equal range of KV tiles per program (StreamPlanArgs below).
 // merge_kernel: LSE-weighted merge of split-KV partials, one warp per output row; replaces the
 //   reference merge prim_funcs (v7.py:317-371, cube_general.py:224-279). Partials carry a base-2
-//   LSE; the empty-split sentinel and validity threshold keep the reference's -1e30 / -1e29.
+//   LSE; the empty-split sentinel and validity threshold keep the reference's -1e30 / -1e29. The
+//   arithmetic is merge_split_* (fgw_common.cuh), shared with the decode kernel's fused merge.
+//   plan_kernel also zeroes the decode kernel's per-group arrival counters when it merges in place.
 #include "fgw_common.cuh"
 #include "fgw_kernels.h"
 
@@ -50,13 +52,16 @@ __device__ __forceinline__ long long stream_program_start(long long total, int p
 
 __global__ void __launch_bounds__(1024) plan_kernel(const int32_t* __restrict__ lengths, int32_t* __restrict__ lens,
                                                    int32_t* __restrict__ order, WorkspaceHeader* ws, int batch,
-                                                   int capacity, StreamPlanArgs sp) {
+                                                   int capacity, StreamPlanArgs sp, int32_t* merge_counters,
+                                                   int merge_groups) {
   extern __shared__ unsigned long long keys[];
   __shared__ long long chunk_sum[1024];
   if (threadIdx.x == 0) {
     ws->error = 0;
     ws->error_site = 0;
   }
+  // the decode kernel's fused split merge counts arrivals per row group from zero
+  for (int i = threadIdx.x; i < merge_groups; i += blockDim.x) merge_counters[i] = 0;
   for (int i = threadIdx.x; i < batch; i += blockDim.x) {
     lens[i] = min(max(lengths[i], 0), capacity);
   }
@@ -174,7 +179,7 @@ cudaError_t launch_plan(const LaunchDesc& d) {
     sp.counters = d.counters;
   }
   plan_kernel<<<1, 1024, smem, d.stream>>>(d.p.cache_seqlens, d.lens, d.order, d.header, batch,
-                                          d.p.table_width * d.p.page_size, sp);
+                                          d.p.table_width * d.p.page_size, sp, d.merge_counters, d.merge_groups);
   return cudaGetLastError();
 }
 
@@ -193,25 +198,20 @@ __global__ void __launch_bounds__(256) merge_kernel(const float* __restrict__ pa
   const float* lse_row = part_lse + row * splits;
   const float* o_row = part_o + row * splits * dim;
   for (int s = 0; s < splits; ++s) {
-    const float lse = lse_row[s];
-    const float next = fmaxf(peak, lse);
-    const float w_old = fast_exp2(peak - next);
-    const float w_new = lse > kValidLse ? fast_exp2(lse - next) : 0.f;
+    float w_old, w_new;
+    merge_split_weights(lse_row[s], peak, total, w_old, w_new);
     const float* src = o_row + s * dim;
 #pragma unroll
     for (int i = 0; i < kMaxPerLane; ++i) {
       const int d = lane + 32 * i;
-      if (d < dim) acc[i] = acc[i] * w_old + (w_new != 0.f ? src[d] * w_new : 0.f);
+      if (d < dim) acc[i] = merge_split_accumulate<false>(acc[i], w_old, w_new, src + d);
     }
-    total = total * w_old + w_new;
-    peak = next;
   }
-  const float inv = 1.f / fmaxf(total, 1e-30f);
   T* dst = out + row * dim;
 #pragma unroll
   for (int i = 0; i < kMaxPerLane; ++i) {
     const int d = lane + 32 * i;
-    if (d < dim) dst[d] = ElemTraits<T>::from_float(acc[i] * inv);
+    if (d < dim) dst[d] = ElemTraits<T>::from_float(merge_split_finish(acc[i], total));
   }
 }
 

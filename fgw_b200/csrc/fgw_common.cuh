@@ -261,6 +261,29 @@ __device__ __forceinline__ float fast_log2(float x) {
   return y;
 }
 
+// LSE-weighted merge of split-KV partials (the reference's merge, v7.py:317-371: running max, rescale,
+// invalid splits weighted 0, denominator clamped at 1e-30), in three steps with every rounding spelled
+// out, so merge_kernel and the decode kernel's fused merge produce the same bits.
+// Split s of a row: updates the running max and weight total, returns the old accumulators' and the new
+// partial's weights.
+__device__ __forceinline__ void merge_split_weights(float lse, float& peak, float& total, float& w_old,
+                                                    float& w_new) {
+  const float next = fmaxf(peak, lse);
+  w_old = fast_exp2(peak - next);
+  w_new = lse > kValidLse ? fast_exp2(lse - next) : 0.f;
+  total = __fmaf_rn(total, w_old, w_new);
+  peak = next;
+}
+// One element's accumulator after split s (the partial is read only when it carries weight; kL2 reads it
+// through L2, for partials other CTAs of the same launch have just written).
+template <bool kL2>
+__device__ __forceinline__ float merge_split_accumulate(float acc, float w_old, float w_new, const float* partial) {
+  return __fmaf_rn(acc, w_old, w_new != 0.f ? __fmul_rn(kL2 ? __ldcg(partial) : *partial, w_new) : 0.f);
+}
+__device__ __forceinline__ float merge_split_finish(float acc, float total) {
+  return __fmul_rn(acc, __fdiv_rn(1.f, fmaxf(total, 1e-30f)));
+}
+
 // ---------------------------------------------------------------------------------------
 // tcgen05: TMEM allocation, UMMA issue/commit, TMEM loads and stores
 // ---------------------------------------------------------------------------------------

@@ -30,6 +30,9 @@ struct DecodeArgs {
   float* part_lse;
   WorkspaceHeader* ws;
   int batch, sq, heads, width, page, splits, causal, row_blocks, box_rows, write_partials;
+  // fused split merge: arrivals per (request, row block, head) group; the CTA completing a group merges it
+  int fused_merge;
+  int32_t* merge_counters;
   long long items;
   float scale_log2;
   uint64_t budget_ns;
@@ -380,6 +383,39 @@ __global__ void __launch_bounds__(DecodeShape<D>::kThreads, 1)
         reinterpret_cast<T*>(a.out)[row_id * D + d] = Tr::from_float(val);
       }
     }
+    if (a.fused_merge) {
+      // Split merge in place: every split's CTA publishes its partial, then counts itself in on the
+      // group's counter; the one whose arrival completes the set merges all the group's partials in
+      // split order (the arithmetic of merge_kernel, so the output is the same bits whichever CTA merges).
+      // No CTA ever waits for another.
+      __shared__ int merge_here;
+      __threadfence();
+      named_barrier_sync(1, consumer_threads);
+      if (threadIdx.x == 0) {
+        const long long g = ((long long)b * a.row_blocks + rb) * a.heads + h;
+        merge_here = atomicAdd(&a.merge_counters[g], 1) == a.splits - 1;
+      }
+      named_barrier_sync(1, consumer_threads);
+      if (merge_here) {
+        __threadfence();
+        for (int idx = threadIdx.x; idx < kRows * D; idx += consumer_threads) {
+          const int r = idx / D;
+          const int d = idx % D;
+          const int qi = q0 + r;
+          if (qi >= a.sq) continue;
+          const long long row_id = ((long long)b * a.sq + qi) * a.heads + h;
+          const float* lse_row = a.part_lse + row_id * a.splits;
+          const float* o_row = a.part_o + row_id * a.splits * D + d;
+          float peak = kEmptyLse, total = 0.f, accm = 0.f;
+          for (int sp = 0; sp < a.splits; ++sp) {
+            float w_old, w_new;
+            merge_split_weights(__ldcg(lse_row + sp), peak, total, w_old, w_new);
+            accm = merge_split_accumulate<true>(accm, w_old, w_new, o_row + (long long)sp * D);
+          }
+          reinterpret_cast<T*>(a.out)[row_id * D + d] = Tr::from_float(merge_split_finish(accm, total));
+        }
+      }
+    }
     named_barrier_sync(1, consumer_threads);
   }
 }
@@ -477,7 +513,7 @@ static bool make_kv_map(CUtensorMap* map, const void* base, const fgw_mha_params
   return r == CUDA_SUCCESS;
 }
 
-cudaError_t launch_decode(const LaunchDesc& d, bool write_partials) {
+cudaError_t launch_decode(const LaunchDesc& d, bool write_partials, bool fused_merge) {
   const fgw_mha_params& p = d.p;
   const int rows = decode_rows_per_item(p.head_dim);
   DecodeArgs args;
@@ -499,6 +535,8 @@ cudaError_t launch_decode(const LaunchDesc& d, bool write_partials) {
   args.row_blocks = (p.q_len + rows - 1) / rows;
   args.box_rows = gcd_int(gcd_int(p.page_size, decode_tile_tokens(p.head_dim)), 256);  // divides page and tile
   args.write_partials = write_partials ? 1 : 0;
+  args.fused_merge = (write_partials && fused_merge && d.merge_counters != nullptr) ? 1 : 0;
+  args.merge_counters = d.merge_counters;
   args.items = (long long)p.batch * args.row_blocks * p.num_splits * p.heads;
   args.scale_log2 = (1.0f / sqrtf((float)p.head_dim)) * kLog2e;
   args.budget_ns = d.budget_ns;

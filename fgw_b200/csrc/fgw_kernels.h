@@ -40,6 +40,10 @@ struct LaunchDesc {
   int32_t* counters;   // [items]
   float* slot_lse;     // [2 * programs, kPairRows] base-2 LSE of each piece row
   float* slot_o;       // [2 * programs, kPairRows, head_dim] FP32 normalised piece outputs
+  // split-KV on the decode path: one arrival counter per (request, row block, head) group, so the CTA that
+  // completes a group's split set merges it in the same launch (zeroed by plan_kernel)
+  int32_t* merge_counters;  // [batch * q_len * heads] (an upper bound on the groups)
+  int merge_groups;         // 0 when there is nothing to zero
   uint64_t budget_ns;
   int sm_count;
   bool single_tile;   // force the one-query-tile tensor kernel (FGW_MHA_TENSOR_SINGLE_TILE set)
@@ -52,7 +56,7 @@ long long pair_items(const fgw_mha_params& p);
 bool use_stream_schedule(const fgw_mha_params& p);
 
 // Workspace layout: header | lens | order | part_lse | part_o | (contiguous schedule: prog_item | prog_off |
-// prog_u | prefix | counters | slot_lse | slot_o), each 256-byte aligned.
+// prog_u | prefix | counters | slot_lse | slot_o) | (split decode: merge_counters), each 256-byte aligned.
 size_t workspace_bytes(const fgw_mha_params& p, int path);
 void carve_workspace(LaunchDesc& d, void* workspace, int path);
 
@@ -61,7 +65,8 @@ void carve_workspace(LaunchDesc& d, void* workspace, int path);
 int gather_validate(const fgw_gather_params& p);
 cudaError_t launch_gather(const fgw_gather_params& p, int sm_count, cudaStream_t stream);
 cudaError_t launch_plan(const LaunchDesc& d);
-cudaError_t launch_decode(const LaunchDesc& d, bool write_partials);
+// fused_merge (with write_partials): the CTA completing a group's split set merges it into the output.
+cudaError_t launch_decode(const LaunchDesc& d, bool write_partials, bool fused_merge);
 cudaError_t launch_merge(const LaunchDesc& d);
 cudaError_t launch_wait_selftest(WorkspaceHeader* ws, uint64_t budget_ns, int complete, cudaStream_t stream);
 cudaError_t launch_tensor(const LaunchDesc& d, bool write_partials);

@@ -99,3 +99,35 @@ def test_tensor_path_long_causal_tails(dim, page):
     inputs = {"case": case, "seed": 2026, "dtype": torch.float16, "causal": True, "pattern": "edge", "q": q,
               "k": k, "v": v, "table": table, "lengths": torch.tensor(lengths, dtype=torch.int32)}
     _check(_run(inputs, path="tensor"), oracle_output(inputs), inputs)
+
+
+@pytest.mark.parametrize("case,splits,causal,pattern,dtype", [
+    (("merge_d128", 4, 1, 8, 128, 64, 40), 4, False, "mixed", torch.bfloat16),
+    (("merge_rows", 3, 5, 4, 128, 16, 100), 16, True, "mixed", torch.bfloat16),
+    (("merge_d64", 8, 2, 16, 64, 128, 12), 2, False, "full", torch.float16),
+    (("merge_d256", 2, 1, 2, 256, 64, 24), 8, True, "mixed", torch.bfloat16),
+    (("merge_groups", 64, 1, 32, 128, 64, 16), 4, False, "mixed", torch.float16),
+], ids=lambda v: v[0] if isinstance(v, tuple) else None)
+def test_decode_split_merge_in_place_matches_the_merge_launch(case, splits, causal, pattern, dtype):
+    # fgw_mha_paged_fwd merges the decode kernel's splits in place: the CTA whose arrival completes a row
+    # group's split set merges it. fgw_mha_partial + fgw_mha_merge do the same merge in a second launch with
+    # the same arithmetic, so the two outputs are the same bits; a second call on the same workspace (arrival
+    # counters zeroed again by the plan kernel) gives them again. Cases include splits past a request's
+    # KV tiles (empty partials) and empty requests.
+    from fgw_b200.operators.mha.current import build_kernel
+    dev = torch.device("cuda", 0)
+    inputs = build_case(case, 7, dtype, causal, pattern)
+    args = [inputs[key].to(dev) for key in ("q", "k", "v", "table", "lengths")]
+    kernel = build_kernel(case[1], case[2], case[3], case[4], args[1].shape[0], case[6], case[5], causal,
+                          dtype_name(dtype), 0, cube_mode="general", num_splits=splits, path="decode")
+    assert kernel.num_splits == splits
+    ws = kernel.new_workspace(dev)
+    fused = kernel(*args, workspace=ws).clone()
+    again = kernel(*args, workspace=ws)
+    separate_ws = kernel.new_workspace(dev)
+    kernel.partial_kernel(*args, separate_ws)
+    separate = kernel.merge_kernel(*args, separate_ws)
+    torch.cuda.synchronize()
+    assert torch.equal(fused.view(torch.int16), separate.view(torch.int16))
+    assert torch.equal(again.view(torch.int16), fused.view(torch.int16))
+    _check(fused, oracle_output(inputs), inputs)
