@@ -197,14 +197,26 @@ __global__ void __launch_bounds__(256) merge_kernel(const float* __restrict__ pa
   float peak = kEmptyLse, total = 0.f;
   const float* lse_row = part_lse + row * splits;
   const float* o_row = part_o + row * splits * dim;
-  for (int s = 0; s < splits; ++s) {
-    float w_old, w_new;
-    merge_split_weights(lse_row[s], peak, total, w_old, w_new);
-    const float* src = o_row + s * dim;
+  constexpr int kChunk = 4;  // splits whose loads are in flight together
+  for (int s0 = 0; s0 < splits; s0 += kChunk) {
+    float lse[kChunk], o[kChunk][kMaxPerLane];
 #pragma unroll
-    for (int i = 0; i < kMaxPerLane; ++i) {
-      const int d = lane + 32 * i;
-      if (d < dim) acc[i] = merge_split_accumulate<false>(acc[i], w_old, w_new, src + d);
+    for (int c = 0; c < kChunk; ++c) {
+      if (s0 + c < splits) {
+        lse[c] = lse_row[s0 + c];
+        const float* src = o_row + (s0 + c) * dim;
+#pragma unroll
+        for (int i = 0; i < kMaxPerLane; ++i) o[c][i] = lane + 32 * i < dim ? src[lane + 32 * i] : 0.f;
+      }
+    }
+#pragma unroll
+    for (int c = 0; c < kChunk; ++c) {
+      if (s0 + c < splits) {
+        float w_old, w_new;
+        merge_split_weights(lse[c], peak, total, w_old, w_new);
+#pragma unroll
+        for (int i = 0; i < kMaxPerLane; ++i) acc[i] = merge_split_accumulate(acc[i], w_old, w_new, o[c][i]);
+      }
     }
   }
   T* dst = out + row * dim;

@@ -274,11 +274,11 @@ __device__ __forceinline__ void merge_split_weights(float lse, float& peak, floa
   total = __fmaf_rn(total, w_old, w_new);
   peak = next;
 }
-// One element's accumulator after split s (the partial is read only when it carries weight; kL2 reads it
-// through L2, for partials other CTAs of the same launch have just written).
-template <bool kL2>
-__device__ __forceinline__ float merge_split_accumulate(float acc, float w_old, float w_new, const float* partial) {
-  return __fmaf_rn(acc, w_old, w_new != 0.f ? __fmul_rn(kL2 ? __ldcg(partial) : *partial, w_new) : 0.f);
+// One element's accumulator after split s (the partial value counts only when it carries weight). Callers
+// load a chunk of splits' LSEs and partial values with independent loads first, then apply the steps in
+// split order, so the loads overlap instead of forming a chain through the weights.
+__device__ __forceinline__ float merge_split_accumulate(float acc, float w_old, float w_new, float partial) {
+  return __fmaf_rn(acc, w_old, w_new != 0.f ? __fmul_rn(partial, w_new) : 0.f);
 }
 __device__ __forceinline__ float merge_split_finish(float acc, float total) {
   return __fmul_rn(acc, __fdiv_rn(1.f, fmaxf(total, 1e-30f)));

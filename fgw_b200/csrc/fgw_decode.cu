@@ -406,11 +406,26 @@ __global__ void __launch_bounds__(DecodeShape<D>::kThreads, 1)
           const long long row_id = ((long long)b * a.sq + qi) * a.heads + h;
           const float* lse_row = a.part_lse + row_id * a.splits;
           const float* o_row = a.part_o + row_id * a.splits * D + d;
+          // through L2 (ld.global.cg): other CTAs of this launch wrote these partials
           float peak = kEmptyLse, total = 0.f, accm = 0.f;
-          for (int sp = 0; sp < a.splits; ++sp) {
-            float w_old, w_new;
-            merge_split_weights(__ldcg(lse_row + sp), peak, total, w_old, w_new);
-            accm = merge_split_accumulate<true>(accm, w_old, w_new, o_row + (long long)sp * D);
+          constexpr int kChunk = 8;  // splits whose loads are in flight together
+          for (int s0 = 0; s0 < a.splits; s0 += kChunk) {
+            float lse[kChunk], o[kChunk];
+#pragma unroll
+            for (int c = 0; c < kChunk; ++c) {
+              if (s0 + c < a.splits) {
+                lse[c] = __ldcg(lse_row + s0 + c);
+                o[c] = __ldcg(o_row + (long long)(s0 + c) * D);
+              }
+            }
+#pragma unroll
+            for (int c = 0; c < kChunk; ++c) {
+              if (s0 + c < a.splits) {
+                float w_old, w_new;
+                merge_split_weights(lse[c], peak, total, w_old, w_new);
+                accm = merge_split_accumulate(accm, w_old, w_new, o[c]);
+              }
+            }
           }
           reinterpret_cast<T*>(a.out)[row_id * D + d] = Tr::from_float(merge_split_finish(accm, total));
         }

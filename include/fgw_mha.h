@@ -140,7 +140,9 @@ FGW_API int fgw_mha_resolve_path(const fgw_mha_params* params, int* path);
 /* Bytes of device workspace fgw_mha_paged_fwd / fgw_mha_partial need for these parameters. */
 FGW_API int fgw_mha_workspace_size(const fgw_mha_params* params, size_t* bytes);
 
-/* Full forward: direct output when num_splits == 1, otherwise partial + merge, on `stream`.
+/* Full forward: direct output when num_splits == 1, otherwise split partials merged into the output (on
+ * the decode path by the kernel itself, the CTA completing a row group's splits merging them; on the
+ * tensor path by a merge launch), on `stream`.
  * `workspace` must be 256-byte aligned device memory of at least fgw_mha_workspace_size bytes.
  * The workspace header's error word is cleared at the start of every call. */
 FGW_API int fgw_mha_paged_fwd(const fgw_mha_params* params, void* workspace, size_t workspace_bytes, void* stream);
