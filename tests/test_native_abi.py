@@ -83,6 +83,20 @@ def test_workspace_size_grows_with_splits():
         _native.workspace_size(_params(batch=0))
 
 
+def test_split_decode_workspace_holds_one_arrival_counter_per_row():
+    # the decode path merges its splits in place: one int32 counter per output row group, upper-bounded by the
+    # rows (a 256-byte aligned region after the partials); the tensor path keeps its merge launch, no counters
+    rows = 8 * 3 * 4
+    shape = dict(batch=8, q_len=3, heads=4, num_splits=4)
+    decode = _native.workspace_size(_params(path=_native.PATH_DECODE, **shape))
+    tensor = _native.workspace_size(_params(path=_native.PATH_TENSOR, **shape))
+    assert decode - tensor == -(-rows * 4 // 256) * 256
+    single = dict(shape, num_splits=1)
+    assert (_native.workspace_size(_params(path=_native.PATH_DECODE, **single))
+            == _native.workspace_size(_params(path=_native.PATH_TENSOR, schedule=_native.SCHEDULE_STRIDED,
+                                              **single)))
+
+
 @pytest.mark.parametrize("override", [dict(head_dim=24), dict(head_dim=272), dict(page_size=24),
                                       dict(pool_rows=500), dict(num_splits=0), dict(dtype=7), dict(causal=2),
                                       dict(path=9)])
