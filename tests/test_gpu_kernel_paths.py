@@ -101,14 +101,18 @@ def test_tensor_path_long_causal_tails(dim, page):
     _check(_run(inputs, path="tensor"), oracle_output(inputs), inputs)
 
 
-@pytest.mark.parametrize("case,splits,causal,pattern,dtype", [
-    (("merge_d128", 4, 1, 8, 128, 64, 40), 4, False, "mixed", torch.bfloat16),
-    (("merge_rows", 3, 5, 4, 128, 16, 100), 16, True, "mixed", torch.bfloat16),
-    (("merge_d64", 8, 2, 16, 64, 128, 12), 2, False, "full", torch.float16),
-    (("merge_d256", 2, 1, 2, 256, 64, 24), 8, True, "mixed", torch.bfloat16),
-    (("merge_groups", 64, 1, 32, 128, 64, 16), 4, False, "mixed", torch.float16),
+@pytest.mark.parametrize("case,splits,causal,pattern,dtype,programs", [
+    (("merge_d128", 4, 1, 8, 128, 64, 40), 4, False, "mixed", torch.bfloat16, None),
+    (("merge_rows", 3, 5, 4, 128, 16, 100), 16, True, "mixed", torch.bfloat16, None),
+    (("merge_d64", 8, 2, 16, 64, 128, 12), 2, False, "full", torch.float16, None),
+    (("merge_d256", 2, 1, 2, 256, 64, 24), 8, True, "mixed", torch.bfloat16, None),
+    (("merge_groups", 64, 1, 32, 128, 64, 16), 4, False, "mixed", torch.float16, None),
+    # 3 heads on 3 programs: every split of a row group is an item of the same CTA, which counts itself in
+    # once per split and merges on the last; and one program doing everything
+    (("merge_one_cta", 2, 1, 3, 128, 128, 16), 8, False, "mixed", torch.bfloat16, 3),
+    (("merge_one_program", 3, 1, 2, 128, 128, 8), 4, True, "full", torch.bfloat16, 1),
 ], ids=lambda v: v[0] if isinstance(v, tuple) else None)
-def test_decode_split_merge_in_place_matches_the_merge_launch(case, splits, causal, pattern, dtype):
+def test_decode_split_merge_in_place_matches_the_merge_launch(case, splits, causal, pattern, dtype, programs):
     # fgw_mha_paged_fwd merges the decode kernel's splits in place: the CTA whose arrival completes a row
     # group's split set merges it. fgw_mha_partial + fgw_mha_merge do the same merge in a second launch with
     # the same arithmetic, so the two outputs are the same bits; a second call on the same workspace (arrival
@@ -118,9 +122,13 @@ def test_decode_split_merge_in_place_matches_the_merge_launch(case, splits, caus
     dev = torch.device("cuda", 0)
     inputs = build_case(case, 7, dtype, causal, pattern)
     args = [inputs[key].to(dev) for key in ("q", "k", "v", "table", "lengths")]
+    # the general route takes only its default program cap; the BF16 D128 page-128 route takes any cap
+    extra = dict(cube_mode="general") if programs is None else dict(persistent_programs=programs)
     kernel = build_kernel(case[1], case[2], case[3], case[4], args[1].shape[0], case[6], case[5], causal,
-                          dtype_name(dtype), 0, cube_mode="general", num_splits=splits, path="decode")
+                          dtype_name(dtype), 0, num_splits=splits, path="decode", **extra)
     assert kernel.num_splits == splits
+    if programs is not None:
+        assert kernel.compute_grid == programs
     ws = kernel.new_workspace(dev)
     fused = kernel(*args, workspace=ws).clone()
     again = kernel(*args, workspace=ws)
