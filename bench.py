@@ -567,73 +567,82 @@ def cpu_longq_sample(budget_s=12.0):
 
 
 # ---------------------------------------------------------------------------------------- reference arm
+# split counts: the B200 model's candidates (general_split_cost_model.B200_SPLITS), each up to the KV tiles;
+# beyond config 3's grid, one request and head over a 128K-token cache (where 64 / 128 splits pay off)
 SWEEP = dict(shapes=((1, 1), (2, 8)), dtypes=("float16", "bfloat16"), queries=(1, 4, 16, 64, 512),
-             kvs=(512, 2048, 8192, 32768), splits=(1, 2, 4, 8, 16, 32), dim=128, page=128)
+             kvs=(512, 2048, 8192, 32768), dim=128, page=128, long=((1, 1, 131072, (1, 4)),))
 
 
 def run_split_sweep(args, device, stream):
     """Config 3: every (B, H) x dtype x Q x KV of the reference's split sweep, full caches, page 128, N(0,1)
-    data; for each split count the call accepts, the median of 5 timings of 20 calls replayed from a CUDA
-    graph (plan + attend + merge; warm L2, as the reference's scan). Rows in the split-model fitter's format."""
+    data; for each candidate split count up to the KV tiles, the median of 5 timings of 20 calls replayed from a
+    CUDA graph (plan + attend + merge; warm L2, as the reference's scan). Rows in the split-model fitter's format."""
     from fgw_b200.operators.mha.current import build_kernel
+    from fgw_b200.operators.mha.general_split_cost_model import B200_SPLITS
     c = SWEEP
     rows = []
-    for (b, h) in c["shapes"]:
-        for kv in c["kvs"]:
-            width = kv // c["page"]
-            g = torch.Generator(device=device).manual_seed(31 + b + kv)
-            pool = b * width
-            table = torch.randperm(pool, device=device, generator=g)[:pool].reshape(b, width).int()
-            lengths = torch.full((b,), kv, dtype=torch.int32, device=device)
-            kf = torch.randn(pool * c["page"], h, c["dim"], device=device, generator=g)
-            vf = torch.randn(pool * c["page"], h, c["dim"], device=device, generator=g)
-            for dtype in c["dtypes"]:
-                tdtype = getattr(torch, dtype)
-                k, v = kf.to(tdtype), vf.to(tdtype)
-                for sq in c["queries"]:
-                    q = torch.randn(b, sq, h, c["dim"], device=device, generator=g).to(tdtype)
-                    # FP16 takes the general route (the default FP16 route accepts no explicit split count)
-                    mode = "general" if dtype == "float16" else "stable"
-                    auto = build_kernel(b, sq, h, c["dim"], pool * c["page"], width, c["page"], False, dtype,
-                                        device.index, full_kv_cache=True, cache_lengths=(kv,) * b, cube_mode=mode)
-                    median = {}
-                    for splits in c["splits"]:
+    grid = [(b, h, kv, c["queries"]) for (b, h) in c["shapes"] for kv in c["kvs"]] + list(c["long"])
+    for (b, h, kv, queries) in grid:
+        width = kv // c["page"]
+        g = torch.Generator(device=device).manual_seed(31 + b + kv)
+        pool = b * width
+        table = torch.randperm(pool, device=device, generator=g)[:pool].reshape(b, width).int()
+        lengths = torch.full((b,), kv, dtype=torch.int32, device=device)
+        kf = torch.randn(pool * c["page"], h, c["dim"], device=device, generator=g)
+        vf = torch.randn(pool * c["page"], h, c["dim"], device=device, generator=g)
+        for dtype in c["dtypes"]:
+            tdtype = getattr(torch, dtype)
+            k, v = kf.to(tdtype), vf.to(tdtype)
+            for sq in queries:
+                q = torch.randn(b, sq, h, c["dim"], device=device, generator=g).to(tdtype)
+                # FP16 takes the general route (the default FP16 route accepts no explicit split count)
+                mode = "general" if dtype == "float16" else "stable"
+                auto = build_kernel(b, sq, h, c["dim"], pool * c["page"], width, c["page"], False, dtype,
+                                    device.index, full_kv_cache=True, cache_lengths=(kv,) * b, cube_mode=mode)
+                median = {}
+                for splits in B200_SPLITS:
+                    # the route's explicit num_splits where it takes the count, else the B200 measurement
+                    # hook (64 / 128, and 32 on the BF16 route, are candidates of the B200 model only)
+                    kernel = None
+                    for how in (dict(num_splits=splits), dict(_b200_splits=splits)):
                         try:
                             kernel = build_kernel(b, sq, h, c["dim"], pool * c["page"], width, c["page"], False,
-                                                  dtype, device.index, num_splits=splits, full_kv_cache=True,
-                                                  cube_mode=mode)
+                                                  dtype, device.index, full_kv_cache=True, cube_mode=mode, **how)
+                            break
                         except ValueError:
-                            continue  # more splits than KV tiles, or a split count this route does not take
-                        ws = kernel.new_workspace(device)
-                        out = torch.empty_like(q)
-                        a = (q, k, v, table, lengths)
-                        for _ in range(3):
+                            continue
+                    if kernel is None:
+                        continue  # more splits than KV tiles
+                    ws = kernel.new_workspace(device)
+                    out = torch.empty_like(q)
+                    a = (q, k, v, table, lengths)
+                    for _ in range(3):
+                        kernel(*a, out=out, workspace=ws)
+                    torch.cuda.synchronize()
+                    graph = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(graph):
+                        for _ in range(20):
                             kernel(*a, out=out, workspace=ws)
+                    times = []
+                    for _ in range(6):
+                        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                        e0.record(stream)
+                        graph.replay()
+                        e1.record(stream)
                         torch.cuda.synchronize()
-                        graph = torch.cuda.CUDAGraph()
-                        with torch.cuda.graph(graph):
-                            for _ in range(20):
-                                kernel(*a, out=out, workspace=ws)
-                        times = []
-                        for _ in range(6):
-                            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                            e0.record(stream)
-                            graph.replay()
-                            e1.record(stream)
-                            torch.cuda.synchronize()
-                            times.append(e0.elapsed_time(e1) * 1e3 / 20)
-                        median[str(splits)] = statistics.median(times[1:])
-                        del graph
-                    if not median:
-                        continue
-                    best = min(median, key=median.get)
-                    rows.append({"case": f"B{b}H{h}_Q{sq}_KV{kv}", "key": f"B{b}H{h}_Q{sq}_KV{kv}_{dtype}",
-                                 "B": b, "Q": sq, "H": h, "D": c["dim"], "dtype": dtype, "page_size": c["page"],
-                                 "table_width": width, "lengths": [kv] * b, "median_us": median,
-                                 "auto_num_splits": auto.num_splits, "split_policy": auto.split_policy,
-                                 "best_num_splits": int(best),
-                                 "auto_relative_to_best": median.get(str(auto.num_splits), float("nan"))
-                                 / median[best]})
+                        times.append(e0.elapsed_time(e1) * 1e3 / 20)
+                    median[str(splits)] = statistics.median(times[1:])
+                    del graph
+                if not median:
+                    continue
+                best = min(median, key=median.get)
+                rows.append({"case": f"B{b}H{h}_Q{sq}_KV{kv}", "key": f"B{b}H{h}_Q{sq}_KV{kv}_{dtype}",
+                             "B": b, "Q": sq, "H": h, "D": c["dim"], "dtype": dtype, "page_size": c["page"],
+                             "table_width": width, "lengths": [kv] * b, "median_us": median,
+                             "auto_num_splits": auto.num_splits, "split_policy": auto.split_policy,
+                             "best_num_splits": int(best),
+                             "auto_relative_to_best": median.get(str(auto.num_splits), float("nan"))
+                             / median[best]})
     return rows
 
 

@@ -197,7 +197,7 @@ __global__ void __launch_bounds__(256) merge_kernel(const float* __restrict__ pa
   float peak = kEmptyLse, total = 0.f;
   const float* lse_row = part_lse + row * splits;
   const float* o_row = part_o + row * splits * dim;
-  constexpr int kChunk = 4;  // splits whose loads are in flight together
+  constexpr int kChunk = 8;  // splits whose loads are in flight together
   for (int s0 = 0; s0 < splits; s0 += kChunk) {
     float lse[kChunk], o[kChunk][kMaxPerLane];
 #pragma unroll

@@ -408,7 +408,7 @@ __global__ void __launch_bounds__(DecodeShape<D>::kThreads, 1)
           const float* o_row = a.part_o + row_id * a.splits * D + d;
           // through L2 (ld.global.cg): other CTAs of this launch wrote these partials
           float peak = kEmptyLse, total = 0.f, accm = 0.f;
-          constexpr int kChunk = 8;  // splits whose loads are in flight together
+          constexpr int kChunk = 16;  // splits whose loads are in flight together
           for (int s0 = 0; s0 < a.splits; s0 += kChunk) {
             float lse[kChunk], o[kChunk];
 #pragma unroll

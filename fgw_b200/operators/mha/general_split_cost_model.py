@@ -19,7 +19,9 @@ describes the B200 kernels instead of the Ascend ones: query rows per work item 
 (``decode_rows``) for up to 8 query rows and 256-row pairs above, KV tiles have 128 tokens, serial work
 per program is counted separately for the two kernels, and with one split a tensor-path launch whose items
 fill fewer than 2/3 of the programs runs the contiguous schedule (KV tiles spread evenly over the
-programs).
+programs). Its candidates are ``B200_SPLITS``: the reference's counts plus 64 and 128, since one request
+and head over a long cache fills only ``splits`` of the 148 SMs (B1 H1 Q1 KV131072 measured 58 us at 32
+splits, 33 us at 128). Explicit ``num_splits`` keeps the reference's accepted set.
 """
 import functools
 import json
@@ -27,6 +29,8 @@ import math
 import pathlib
 
 from fgw_b200.operators.mha.general_split_policy import SPLITS
+
+B200_SPLITS = SPLITS + (64, 128)  # candidates of the version-3 (B200) model
 
 MODEL_DIR = pathlib.Path(__file__).with_name("models")
 FEATURE_NAMES = (
@@ -113,7 +117,7 @@ def features(batch, sq, heads, dim, lengths, splits, version=1, cores=28):
         raise ValueError("Positive B/Q/H and D16..256 step16 required")
     if len(lengths) != batch or any(type(n) is not int or n < 0 for n in lengths):
         raise ValueError("One nonnegative integer cache length per request required")
-    if type(splits) is not int or splits not in SPLITS:
+    if type(splits) is not int or splits not in (B200_SPLITS if version == 3 else SPLITS):
         raise ValueError("Unsupported split count")
     if version == 3:
         return _features_b200(batch, sq, heads, dim, lengths, splits, cores)
@@ -161,7 +165,7 @@ def select_model_splits(batch, sq, heads, dim, page_size, width, lengths, model=
     tile = KV_TILE if model["version"] == 3 else 32
     capacity_tiles = (page_size * width + tile - 1) // tile
     costs = {}
-    for s in SPLITS:
+    for s in (B200_SPLITS if model["version"] == 3 else SPLITS):
         if s <= capacity_tiles:
             costs[s] = predict_us(batch, sq, heads, dim, lengths, s, model, cores=cores)
     best = min(costs.values())

@@ -98,8 +98,13 @@ def build_kernel(batch, sq, heads, dim, pool_rows, width, page_size, causal, dty
                  pipeline_stages=2, buffer_versions=2, q_resident=True, kv_versions=None, dump_ir_dir=None,
                  schedule_mode="manual", num_splits=None, split_policy="auto", full_kv_cache=False,
                  persistent_programs=DEFAULT_PROGRAMS, cube_mode="stable", cache_lengths=None,
-                 general_model_version=1, task_assignment=None, path="auto"):
-    """Validate a static shape, pick the split count and return a launch callable."""
+                 general_model_version=1, task_assignment=None, path="auto", _b200_splits=None):
+    """Validate a static shape, pick the split count and return a launch callable.
+
+    ``_b200_splits`` (B200-only, for measuring the split model's candidates) fixes the split count to one of
+    ``general_split_cost_model.B200_SPLITS``, including the 64 and 128 that ``split_policy="auto"`` may pick but
+    an explicit ``num_splits`` does not accept (the reference's set).
+    """
     if str(dtype) not in ("float16", "torch.float16", "bfloat16", "torch.bfloat16"):
         raise ValueError("FP16 or BF16 required")
     if dim < 16 or dim > 256 or dim % 16:
@@ -138,7 +143,14 @@ def build_kernel(batch, sq, heads, dim, pool_rows, width, page_size, causal, dty
 
     requested_policy = split_policy
     capacity_tokens = width * page_size
-    if selected_route == "cube_general":
+    if _b200_splits is not None:
+        if num_splits is not None or type(_b200_splits) is not int or _b200_splits not in general_model.B200_SPLITS:
+            raise ValueError("_b200_splits takes one of B200_SPLITS, and no num_splits")
+        if _b200_splits > (capacity_tokens + general_model.KV_TILE - 1) // general_model.KV_TILE:
+            raise ValueError("_b200_splits must not exceed the 128-token KV tiles in table capacity")
+        splits = _b200_splits
+        policy_name = "explicit"
+    elif selected_route == "cube_general":
         capacity_tiles = (capacity_tokens + 31) // 32
         tasks = batch * heads * ((sq + 31) // 32)
         if num_splits is None and split_policy == "cost_model":

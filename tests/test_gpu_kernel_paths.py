@@ -139,3 +139,27 @@ def test_decode_split_merge_in_place_matches_the_merge_launch(case, splits, caus
     assert torch.equal(fused.view(torch.int16), separate.view(torch.int16))
     assert torch.equal(again.view(torch.int16), fused.view(torch.int16))
     _check(fused, oracle_output(inputs), inputs)
+
+
+@pytest.mark.parametrize("splits,dtype", [(64, torch.bfloat16), (128, torch.float16)])
+def test_b200_split_counts_beyond_the_reference_set(splits, dtype):
+    # The B200 split model may pick 64 or 128 splits (one request and head over a long cache fills only
+    # `splits` SMs); an explicit num_splits keeps the reference's accepted set. Long ragged caches, many
+    # empty splits for the short request; in-place merge against the merge launch and the oracle.
+    from fgw_b200.operators.mha.current import build_kernel
+    case = ("many_splits", 2, 1, 2, 128, 128, 160)  # table capacity 20480 tokens = 160 KV tiles
+    dev = torch.device("cuda", 0)
+    inputs = build_case(case, 42, dtype, False, "mixed")
+    args = [inputs[key].to(dev) for key in ("q", "k", "v", "table", "lengths")]
+    shape = (case[1], case[2], case[3], case[4], args[1].shape[0], case[6], case[5], False, dtype_name(dtype), 0)
+    with pytest.raises(ValueError):
+        build_kernel(*shape, cube_mode="general", num_splits=splits)
+    kernel = build_kernel(*shape, _b200_splits=splits, path="decode")
+    assert kernel.num_splits == splits
+    fused = kernel(*args)
+    separate_ws = kernel.new_workspace(dev)
+    kernel.partial_kernel(*args, separate_ws)
+    separate = kernel.merge_kernel(*args, separate_ws)
+    torch.cuda.synchronize()
+    assert torch.equal(fused.view(torch.int16), separate.view(torch.int16))
+    _check(fused, oracle_output(inputs), inputs)

@@ -104,6 +104,20 @@ def test_b200_features_by_hand():
     assert f[2] == 6.0 and f[4] == 1.0 and f[8] == 8 - 6.0
     with pytest.raises(ValueError):
         gm.features(1, 1, 1, 128, [2048], 3, version=3)
+    # the B200 candidates go past the reference's 32 (one request and head over a long cache); versions 1 and 2
+    # keep the reference's set
+    f = gm.features(1, 1, 1, 128, [131072], 64, version=3, cores=148)
+    assert f[:7] == [1.0, 16.0, 0.0, 1.0, 0.0, 1.0, 64.0]
+    assert gm.B200_SPLITS == (1, 2, 4, 8, 16, 32, 64, 128)
+    with pytest.raises(ValueError):
+        gm.features(1, 1, 1, 128, [131072], 64, version=2)
+
+
+def test_b200_model_picks_past_32_splits_on_a_long_single_head_cache():
+    # measured (committed sweep): B1 H1 Q1 KV131072 runs 43 us at 64 splits against 59 at 32 and 97 at 16
+    model = gm.load_model(3)
+    assert gm.select_model_splits(1, 1, 1, 128, 128, 1024, [131072], model=model) == 64
+    assert gm.select_model_splits(2, 1, 8, 128, 128, 256, [32768, 32768], model=model) <= 32
 
 
 def test_b200_model_selection_on_the_sweep():
