@@ -154,6 +154,9 @@ def test_b200_split_counts_beyond_the_reference_set(splits, dtype):
     shape = (case[1], case[2], case[3], case[4], args[1].shape[0], case[6], case[5], False, dtype_name(dtype), 0)
     with pytest.raises(ValueError):
         build_kernel(*shape, cube_mode="general", num_splits=splits)
+    for bad in (dict(_b200_splits=3), dict(_b200_splits=256), dict(_b200_splits=splits, num_splits=2)):
+        with pytest.raises(ValueError):  # not a candidate / past the 160 KV tiles / both ways at once
+            build_kernel(*shape, **bad)
     kernel = build_kernel(*shape, _b200_splits=splits, path="decode")
     assert kernel.num_splits == splits
     fused = kernel(*args)
