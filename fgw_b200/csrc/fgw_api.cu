@@ -1,7 +1,8 @@
 // C ABI of libfgw_mha.so: argument validation, workspace carve-up, path choice and launch order.
 // The host-side control flow mirrors the reference's launch callables (v7.py:471-498,
 // cube_general.py:186-188, 284-288): one launch when there is one split, partial then merge
-// otherwise, all on the caller's stream. A small planning launch precedes them and replaces the
+// otherwise (the decode path merges in the same launch, the CTA completing a row group's splits
+// merging them), all on the caller's stream. A small planning launch precedes them and replaces the
 // reference's host copy of the cache lengths (v7.py:548).
 #include <algorithm>
 #include <cstdlib>
