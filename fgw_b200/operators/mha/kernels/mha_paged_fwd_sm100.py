@@ -138,16 +138,17 @@ def build_kernel(batch, sq, heads, dim, pool_rows, width, page_size, causal, dty
             raise ValueError("K/V L1 versions must be 1, 2 or 3")
         if pipeline_stages not in (1, 2, 3) or buffer_versions not in (1, 2, 3):
             raise ValueError("Experimental pipeline stages and buffer versions must be 1, 2 or 3")
+    if _b200_splits is not None:
+        if num_splits is not None or type(_b200_splits) is not int or _b200_splits not in general_model.B200_SPLITS:
+            raise ValueError("_b200_splits takes one of B200_SPLITS, and no num_splits")
+        if _b200_splits > (width * page_size + general_model.KV_TILE - 1) // general_model.KV_TILE:
+            raise ValueError("_b200_splits must not exceed the 128-token KV tiles in table capacity")
     dev = _device_index(device_index)
     cores = sm_count(dev)
 
     requested_policy = split_policy
     capacity_tokens = width * page_size
     if _b200_splits is not None:
-        if num_splits is not None or type(_b200_splits) is not int or _b200_splits not in general_model.B200_SPLITS:
-            raise ValueError("_b200_splits takes one of B200_SPLITS, and no num_splits")
-        if _b200_splits > (capacity_tokens + general_model.KV_TILE - 1) // general_model.KV_TILE:
-            raise ValueError("_b200_splits must not exceed the 128-token KV tiles in table capacity")
         splits = _b200_splits
         policy_name = "explicit"
     elif selected_route == "cube_general":

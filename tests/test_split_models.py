@@ -144,3 +144,14 @@ def test_work_accounting_matches_the_oracle():
         assert (work.algorithmic_bytes(lengths, len(lengths), 4, 8, 128, 16, 2)
                 == oracle.algorithmic_bytes(lengths, len(lengths), 4, 8, 128, 16, 2))
     assert work.useful_flops([2048, 2048], 4096, 8, 128, False) == 68_719_476_736  # config 2: 68.72 GFLOP
+
+
+@pytest.mark.parametrize("bad", [dict(_b200_splits=3), dict(_b200_splits=256), dict(_b200_splits=64, num_splits=2),
+                                 dict(_b200_splits=128)])
+def test_b200_split_hook_is_checked_before_any_device_use(bad):
+    # build_kernel(_b200_splits=...) times the B200 model's candidates past the reference's set; counts outside
+    # B200_SPLITS, past the table's 128-token KV tiles (here 100 tiles) or given together with num_splits are
+    # refused before the device is touched
+    from fgw_b200.operators.mha.kernels.mha_paged_fwd_sm100 import build_kernel
+    with pytest.raises(ValueError, match="_b200_splits"):
+        build_kernel(1, 1, 1, 128, 128 * 100, 100, 128, False, "bfloat16", 0, **bad)
