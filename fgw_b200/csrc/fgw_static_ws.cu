@@ -10,7 +10,8 @@
 //
 // The array's name is only a host-side stand-in in host code; its device address is looked up once
 // per device with cudaGetSymbolAddress (with that device current) on the first call made on that device,
-// and cached. Nothing here allocates.
+// and cached for the process (a cudaDeviceReset, which reloads the module, would leave it stale; the
+// header says not to call after one). Nothing here allocates.
 #include <mutex>
 
 #include "fgw_mha.h"

@@ -176,7 +176,8 @@ FGW_API int fgw_mha_merge(const fgw_mha_params* params, void* workspace, size_t 
  * library's floating-point tolerance, not bit for bit). Returns FGW_ERR_WORKSPACE_TOO_SMALL when the
  * request still needs more than that size. Counters and the error word that must start at zero are
  * zeroed on the device by each call's first kernel. The first call on a device looks up the array's
- * device address on the current device; make that first call before any stream capture. All calls
+ * device address on the current device and keeps it for the process (a cudaDeviceReset invalidates it: do
+ * not call this entry point after one); make that first call before any stream capture. All calls
  * share the one array, so calls that overlap on the GPU (different streams, or threads) race:
  * serialise them. */
 FGW_API int fgw_mha_paged_fwd_static_ws(const fgw_mha_params* params, void* stream);
