@@ -43,7 +43,7 @@ sys.path.insert(0, str(ROOT))
 METRIC = "µs/call + % roofline (TC TFLOP/s long-Q, HBM GB/s decode) at 1/2/4/8 B200"
 LONGQ = dict(batch=2, sq=4096, heads=8, dim=128, page=128, kv=2048)
 DECODE = dict(batch=256, sq=1, heads=32, dim=128, page=64, kv_lo=1024, kv_hi=32768)
-ASCEND_V7_TFLOPS = 237.4  # v7 persistent28, B2H8 Q4096 KV2048, Ascend 950PR
+ASCEND_V7_TFLOPS = 237.4  # FGW's published figure: v7 persistent28, B2H8 Q4096 KV2048, Ascend 950PR
 FLUSH_BYTES = 256 << 20
 
 
@@ -737,7 +737,7 @@ def main(argv=None):
                        "seq_len": c["sq"], "kv_len": c["kv"], "parallelism": f"batch-shard x{world}",
                        "l2": "flushed (256 MiB write) before every timed step", "num_splits": k.num_splits,
                        "execution_path": k.execution_path, "compute_grid": k.compute_grid,
-                       "vs_baseline_source": "BASELINE.md: 237.4 TFLOP/s, FGW v7 persistent28 on Ascend 950PR "
+                       "vs_baseline_source": "published: 237.4 TFLOP/s, FGW v7 persistent28 on Ascend 950PR "
                                              "(per GPU)"},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": tc_peak, "unit": "TFLOP/s",
                          "frac": achieved / tc_peak, "traffic": traffic,

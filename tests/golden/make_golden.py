@@ -1,8 +1,8 @@
 """Generate the golden fixtures that pin the oracle and the split selectors to FGW itself.
 
-Run once in a checkout that has the reference at ``--reference`` (default ``/root/reference``):
+Run once, pointing ``--reference`` at a checkout of FGW:
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py --reference <FGW checkout>
 
 It needs the reference's own Python code but none of its NPU stack:
 
@@ -170,7 +170,7 @@ def make_flops(ref_root):
 
 def main(argv=None):
     parser = argparse.ArgumentParser(description=__doc__)
-    parser.add_argument("--reference", default="/root/reference")
+    parser.add_argument("--reference", required=True, help="path of an FGW checkout")
     args = parser.parse_args(argv)
     ref_root = pathlib.Path(args.reference)
     print("outputs", make_outputs(ref_root))

@@ -1,8 +1,8 @@
 """Generate ``static_schedule.json``: FGW's host static schedules over a shape grid, for parity tests.
 
-Run once in a checkout that has the reference at ``--reference`` (default ``/root/reference``):
+Run once, pointing ``--reference`` at a checkout of FGW:
 
-    python tests/golden/make_schedule_golden.py
+    python tests/golden/make_schedule_golden.py --reference <FGW checkout>
 
 ``operators/mha/static_schedule.py`` of the reference is stdlib-only and is imported directly. Every plan
 (programs of segments ``[q_tile, first_kv_block, kv_blocks, slot]``, merges, partial count, strategy) and
@@ -42,7 +42,7 @@ def plan_record(plan):
 
 def main():
     parser = argparse.ArgumentParser()
-    parser.add_argument("--reference", default="/root/reference")
+    parser.add_argument("--reference", required=True, help="path of an FGW checkout")
     args = parser.parse_args()
     ref = load(args.reference)
     out = {"make_plan": {}, "make_q_plan": {}, "make_tail_plan": {}, "make_stream_plan": {}, "choose_plan": {},
