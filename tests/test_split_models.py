@@ -155,3 +155,31 @@ def test_b200_split_hook_is_checked_before_any_device_use(bad):
     from fgw_b200.operators.mha.kernels.mha_paged_fwd_sm100 import build_kernel
     with pytest.raises(ValueError, match="_b200_splits"):
         build_kernel(1, 1, 1, 128, 128 * 100, 100, 128, False, "bfloat16", 0, **bad)
+
+
+def test_b200_model_choice_is_a_candidate_within_the_table_capacity():
+    import random
+    model = gm.load_model(3)
+    rng = random.Random(7)
+    for _ in range(300):
+        batch, heads = rng.choice([1, 2, 4, 16, 64]), rng.choice([1, 2, 8, 32])
+        sq = rng.choice([1, 3, 8, 16, 128, 512, 4096])
+        dim, page = rng.choice([16, 64, 128, 256]), rng.choice([16, 64, 128])
+        width = rng.choice([1, 2, 7, 64, 512])
+        lengths = [rng.randrange(0, page * width + 1) for _ in range(batch)]
+        pick = gm.select_model_splits(batch, sq, heads, dim, page, width, lengths, model=model, cores=148)
+        assert pick in gm.B200_SPLITS and pick <= max(1, -(-page * width // gm.KV_TILE))
+
+
+def test_fit_cli_reproduces_the_shipped_model(tmp_path):
+    import json
+    import pathlib
+    from fgw_b200.operators.mha import fit_split_cost_model
+    sweep = pathlib.Path(__file__).resolve().parent / "golden" / "b200_split_sweep.json"
+    out = tmp_path / "model.json"
+    assert fit_split_cost_model.main(["--input", str(sweep), "--output", str(out), "--version", "3"]) == 0
+    fitted = json.loads(out.read_text())
+    shipped = gm.load_model(3)
+    assert fitted["feature_names"] == shipped["feature_names"]
+    assert fitted["training_rows"] == shipped["training_rows"]
+    assert fitted["weights"] == pytest.approx(shipped["weights"], rel=1e-9, abs=1e-12)
