@@ -40,6 +40,15 @@ static bool single_tile_requested() {
   return value;
 }
 
+// Opt-in key-halves tensor kernel (fgw_fmha_halves_sm100.cu): FGW_MHA_TENSOR_KERNEL=halves.
+static bool key_halves_requested() {
+  static const bool value = [] {
+    const char* v = std::getenv("FGW_MHA_TENSOR_KERNEL");
+    return v != nullptr && std::strcmp(v, "halves") == 0;
+  }();
+  return value;
+}
+
 long long pair_items(const fgw_mha_params& p) {
   return static_cast<long long>(p.batch) * p.heads * p.num_splits * ((p.q_len + kPairRows - 1) / kPairRows);
 }
@@ -50,7 +59,7 @@ long long pair_items(const fgw_mha_params& p) {
 bool use_stream_schedule(const fgw_mha_params& p) {
   if (p.schedule == FGW_SCHEDULE_STRIDED) return false;
   const bool applies = resolve_path(p) == FGW_PATH_TENSOR && p.head_dim <= 128 && p.num_splits == 1 &&
-                       !single_tile_requested() && pair_items(p) <= kStreamMaxItems;
+                       !single_tile_requested() && !key_halves_requested() && pair_items(p) <= kStreamMaxItems;
   if (!applies) return false;
   return p.schedule == FGW_SCHEDULE_CONTIGUOUS || p.schedule == FGW_SCHEDULE_TAIL ||
          3 * pair_items(p) < 2ll * kStreamMaxPrograms;
@@ -209,6 +218,7 @@ static int prepare(const fgw_mha_params* params, void* workspace, size_t workspa
   d.budget_ns = static_cast<uint64_t>(budget_ms) * 1000000ull;
   d.stream = static_cast<cudaStream_t>(stream);
   d.single_tile = single_tile_requested();
+  d.key_halves = key_halves_requested() && !d.single_tile;
   if (d.contiguous) {
     const int cap = d.p.grid_cap > 0 ? d.p.grid_cap : d.sm_count;
     d.programs = std::min(std::min(cap, d.sm_count), kStreamMaxPrograms);

@@ -47,6 +47,7 @@ struct LaunchDesc {
   uint64_t budget_ns;
   int sm_count;
   bool single_tile;   // force the one-query-tile tensor kernel (FGW_MHA_TENSOR_SINGLE_TILE set)
+  bool key_halves;    // opt-in key-halves tensor kernel for head_dim <= 128 (FGW_MHA_TENSOR_KERNEL=halves)
   cudaStream_t stream;
 };
 
@@ -73,6 +74,9 @@ cudaError_t launch_tensor(const LaunchDesc& d, bool write_partials);
 // Two-query-tile tensor kernel (head_dim <= 128); called by launch_tensor with its tensor maps.
 cudaError_t launch_tensor_pairs(const LaunchDesc& d, bool write_partials, const CUtensorMap& qmap,
                                 const CUtensorMap& kmap, const CUtensorMap& vmap, int box_rows);
+// Key-halves tensor kernel (head_dim <= 128, opt-in); called by launch_tensor with its tensor maps.
+cudaError_t launch_tensor_halves(const LaunchDesc& d, bool write_partials, const CUtensorMap& qmap,
+                                 const CUtensorMap& kmap, const CUtensorMap& vmap, int box_rows);
 
 // Which path AUTO picks.
 int resolve_path(const fgw_mha_params& p);
