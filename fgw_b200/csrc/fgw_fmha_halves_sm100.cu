@@ -1,6 +1,6 @@
 // Tensor-core paged attention with the softmax split by key halves (head dims up to 128). Opt-in:
 // launched only when FGW_MHA_TENSOR_KERNEL=halves is set in the environment; the two-query-tile kernel
-// (fgw_fmha2_sm100.cu) stays the default.
+// (fgw_fmha2_sm100.cu) stays the default, since it is still the faster one on the long-query workload.
 //
 // Same contract, masking rules and epilogues as the other tensor kernels; the reference body it stands for
 // is operators/mha/kernels/mha_paged_decode_ascend_v7.py:225-315, 375-465. What changes is how the softmax
