@@ -1,20 +1,29 @@
-"""Fit the split-count latency model on measured split sweeps (NumPy only; offline, on the host).
+"""Offline fit of the B200 split-count latency model (``general_split_cost_model`` version 3).
 
-Restates the fitting method of FGW's tools/mha/fit_general_split_model.py (:15-64 ``fit``, :67-85
-``evaluate`` / ``summarize``, :88-121 leave-one-shape-out) for the B200 model of
-``general_split_cost_model``:
+The model predicts a launch's latency as ``max(f(shape, splits) . w, floor)`` with nonnegative weights
+``w`` and one floor for single-split and one for multi-split launches. This module estimates ``w`` and the
+floors from split sweeps measured on the GPU (the rows ``bench.py --sweep-splits`` writes).
 
-* every measured (shape, split) latency contributes one row of relative error: features / latency
-  against a target of 1;
-* version 2 and the B200 feature set (version 3) add, per shape, every pairwise split contrast (feature difference against latency
-  difference), scaled by sqrt(0.25 / (splits - 1)) / the shape's best latency, so the fit ranks splits
-  within a shape and is less sensitive to per-session constant offsets;
-* columns are normalised, then nonnegative coordinate descent solves the least squares;
-* the single- and multi-split latency floors are the smallest measured latencies of each kind;
-* validation: calibration on all rows, and leave-one-shape-out (both dtypes of a shape held out together).
+Objective. The loss is the one FGW's fitter minimises (tools/mha/fit_general_split_model.py:15-64), so a
+model fitted here means the same thing as one fitted there:
 
-The input is the row list ``bench.py --sweep-splits`` writes. Selection during evaluation is restricted
-to the split counts a row measured. ``cores`` is the SM count the features are computed for (148).
+* absolute fit, in relative terms: for every measured (shape, split) with latency ``y`` and features ``f``,
+  ``(f . w / y - 1)^2``;
+* ranking within a shape (version >= 2): for a shape that measured ``k`` split counts and whose fastest
+  measurement is ``y_min``, ``0.25 / ((k - 1) * y_min^2)`` times the sum over all pairs of split counts of
+  ``((f_s - f_t) . w - (y_s - y_t))^2``. This term rewards getting the order of a shape's splits right even
+  when a sweep session ran uniformly slow or fast.
+
+Solution method (this module's own). The pairwise term is never formed pair by pair: with
+``e_s = f_s . w - y_s``, the identity ``sum_{s<t} (e_s - e_t)^2 = k * sum_s (e_s - mean(e))^2`` turns a
+shape's ``k (k - 1) / 2`` difference rows into ``k`` centred rows ``sqrt(k c) (f_s - mean f)`` with targets
+``sqrt(k c) (y_s - mean y)``. The stacked system is then solved exactly (no iteration count, no stopping
+tolerance) by Lawson-Hanson active-set nonnegative least squares after equilibrating the columns to unit
+norm, which leaves the nonnegative minimiser unchanged.
+
+Floors are the fastest single- and multi-split measurements in the training rows. Validation reports the
+regret of the model's choice (``general_split_cost_model.pick_within_tolerance`` over the split counts a row
+measured) on the training rows and leave-one-shape-out (a shape's FP16 and BF16 rows held out together).
 
     python -m fgw_b200.operators.mha.fit_split_cost_model --input sweep.json --output model.json
 """
@@ -25,96 +34,88 @@ import math
 import pathlib
 
 import numpy as np
+from scipy.optimize import nnls
 
-from fgw_b200.operators.mha.general_split_cost_model import feature_names, features, predict_us
+from fgw_b200.operators.mha.general_split_cost_model import (feature_names, features, pick_within_tolerance,
+                                                             predict_us)
+
+RANKING_WEIGHT = 0.25       # weight of the within-shape ranking term (version >= 2)
+SELECTION_TOLERANCE = 0.02  # relative tolerance of the split choice
+SELECTION_MARGIN_US = 1.0   # absolute tolerance of the split choice (version >= 2)
 
 
-def _features(row, splits, version, cores):
-    return features(row["B"], row["Q"], row["H"], row["D"], list(row["lengths"]), int(splits), version, cores)
+def _shape_block(row, version, cores):
+    """Feature matrix [k, F] and latencies [k] of one sweep row, in its split-count order."""
+    labels = list(row["median_us"])
+    f = np.array([features(row["B"], row["Q"], row["H"], row["D"], list(row["lengths"]), int(s), version, cores)
+                  for s in labels], dtype=np.float64)
+    y = np.array([row["median_us"][s] for s in labels], dtype=np.float64)
+    return f, y
 
 
-def fit(rows, version=3, cores=148, iterations=8000):
-    """Nonnegative weights, latency floors and selection settings fitted on ``rows``."""
-    x = np.array([_features(r, s, version, cores) for r in rows for s in r["median_us"]], dtype=float)
-    y = np.array([us for r in rows for us in r["median_us"].values()], dtype=float)
-    a = x / y[:, None]
-    target = np.ones(len(y))
-    if version >= 2:
-        contrast_x, contrast_y = [], []
-        for r in rows:
-            values = r["median_us"]
-            labels = list(values)
-            if len(labels) < 2:
-                continue
-            vectors = {s: np.array(_features(r, s, version, cores)) for s in labels}
-            factor = math.sqrt(0.25 / (len(labels) - 1)) / min(values.values())
-            for i, s in enumerate(labels):
-                for t in labels[i + 1:]:
-                    contrast_x.append((vectors[s] - vectors[t]) * factor)
-                    contrast_y.append((values[s] - values[t]) * factor)
-        if contrast_x:
-            a = np.vstack([a, np.array(contrast_x)])
-            target = np.concatenate([target, np.array(contrast_y)])
-    scale = np.maximum(np.linalg.norm(a, axis=0), 1e-12)
-    a = a / scale
-    weights = np.zeros(a.shape[1])
-    residual = target.copy()
-    norms = np.sum(a * a, axis=0)
-    done = 0
-    for done in range(iterations):
-        old = weights.copy()
-        for j in range(len(weights)):
-            update = max(0.0, weights[j] + a[:, j] @ residual / max(norms[j], 1e-20))
-            residual += a[:, j] * (weights[j] - update)
-            weights[j] = update
-        if np.max(np.abs(weights - old)) < 1e-9:
-            break
-    floors = {mode: min(us for r in rows for s, us in r["median_us"].items() if (int(s) > 1) == multi)
-              for mode, multi in (("single", False), ("multi", True))}
+def design(rows, version=3, cores=148):
+    """Stacked least-squares system (matrix, target) whose nonnegative minimiser is the model's weights."""
+    blocks, targets = [], []
+    for row in rows:
+        f, y = _shape_block(row, version, cores)
+        blocks.append(f / y[:, None])
+        targets.append(np.ones_like(y))
+        k = len(y)
+        if version >= 2 and k >= 2:
+            weight = math.sqrt(k * RANKING_WEIGHT / (k - 1)) / y.min()
+            blocks.append(weight * (f - f.mean(axis=0)))
+            targets.append(weight * (y - y.mean()))
+    return np.vstack(blocks), np.concatenate(targets)
+
+
+def latency_floors(rows):
+    single = [us for r in rows for s, us in r["median_us"].items() if int(s) == 1]
+    multi = [us for r in rows for s, us in r["median_us"].items() if int(s) > 1]
+    return {"single": min(single), "multi": min(multi)}
+
+
+def fit(rows, version=3, cores=148):
+    """Model dict (weights, floors, selection settings) fitted on ``rows``."""
+    matrix, target = design(rows, version, cores)
+    norms = np.linalg.norm(matrix, axis=0)
+    norms[norms == 0.0] = 1.0  # a feature that never varies keeps weight 0
+    solution, _ = nnls(matrix / norms, target, maxiter=50 * matrix.shape[1])
     return {"version": version, "cores": cores, "feature_names": list(feature_names(version)),
-            "weights": (weights / scale).tolist(), "latency_floor_us": floors, "selection_tolerance": 0.02,
-            "absolute_selection_margin_us": 1.0 if version >= 2 else 0.0,
-            "contrast_loss_weight": 0.25 if version >= 2 else 0.0, "coordinate_descent_iterations": done + 1}
+            "weights": (solution / norms).tolist(), "latency_floor_us": latency_floors(rows),
+            "selection_tolerance": SELECTION_TOLERANCE,
+            "absolute_selection_margin_us": SELECTION_MARGIN_US if version >= 2 else 0.0,
+            "contrast_loss_weight": RANKING_WEIGHT if version >= 2 else 0.0, "solver": "nnls"}
 
 
-def select_measured(row, model):
-    """The model's split choice among the split counts ``row`` measured (smallest within tolerance)."""
-    costs = {int(s): predict_us(row["B"], row["Q"], row["H"], row["D"], list(row["lengths"]), int(s), model)
-             for s in row["median_us"]}
-    best = min(costs.values())
-    if model["version"] == 1:
-        limit = best * (1 + model["selection_tolerance"])
-    else:
-        limit = best + max(best * model["selection_tolerance"], model.get("absolute_selection_margin_us", 0.0))
-    return min(s for s, value in costs.items() if value <= limit)
+def regrets(rows, model):
+    """Per row: the split the model picks among the measured ones and its slowdown against the fastest."""
+    out = []
+    for row in rows:
+        measured = {int(s): us for s, us in row["median_us"].items()}
+        predicted = {s: predict_us(row["B"], row["Q"], row["H"], row["D"], list(row["lengths"]), s, model)
+                     for s in measured}
+        pick = pick_within_tolerance(predicted, model)
+        out.append({"key": row["key"], "model_splits": pick,
+                    "regret_percent": 100.0 * (measured[pick] / min(measured.values()) - 1.0)})
+    return out
 
 
-def evaluate(rows, model):
-    results = []
-    for r in rows:
-        split = select_measured(r, model)
-        selected = r["median_us"][str(split)]
-        best = min(r["median_us"].values())
-        results.append({"key": r["key"], "model_splits": split, "regret_percent": (selected / best - 1) * 100})
-    return results
-
-
-def summarize(results):
-    regrets = [r["regret_percent"] for r in results]
-    return {"cases": len(results), "within_2pct": sum(v <= 2 for v in regrets), "max_regret_percent": max(regrets),
-            "geomean_regret_percent": (math.exp(sum(math.log1p(v / 100) for v in regrets) / len(regrets)) - 1) * 100,
+def summary(results):
+    values = np.array([r["regret_percent"] for r in results], dtype=np.float64)
+    return {"cases": int(values.size), "within_2pct": int(np.count_nonzero(values <= 2.0)),
+            "max_regret_percent": float(values.max()),
+            "geomean_regret_percent": float(100.0 * (np.exp(np.mean(np.log1p(values / 100.0))) - 1.0)),
             "results": results}
 
 
 def fit_and_validate(rows, version=3, cores=148):
-    """The fitted model with its calibration and leave-one-shape-out summaries attached."""
+    """The fitted model with its training-set and leave-one-shape-out regret summaries."""
     model = fit(rows, version, cores)
-    folds = []
+    held_out = []
     for shape in sorted({r["case"] for r in rows}):
-        train = [r for r in rows if r["case"] != shape]
-        held = [r for r in rows if r["case"] == shape]
-        folds.extend(evaluate(held, fit(train, version, cores)))
-    model["validation"] = {"calibration": summarize(evaluate(rows, model)), "leave_one_shape_out": summarize(folds)}
+        trained = fit([r for r in rows if r["case"] != shape], version, cores)
+        held_out += regrets([r for r in rows if r["case"] == shape], trained)
+    model["validation"] = {"calibration": summary(regrets(rows, model)), "leave_one_shape_out": summary(held_out)}
     return model
 
 
@@ -127,20 +128,18 @@ def main(argv=None):
     args = parser.parse_args(argv)
     source = pathlib.Path(args.input)
     data = json.loads(source.read_text(encoding="utf-8"))
-    model = fit_and_validate(data["rows"], args.version, args.cores)
-    model = {"model": f"b200_general_v{args.version}", "status": "fitted on B200 split sweeps", **model,
-             "hardware": data.get("gpu", "unknown"),
-             "training_sha256": hashlib.sha256(source.read_bytes()).hexdigest(),
-             "training_rows": len(data["rows"]), "training_shapes": len({r["case"] for r in data["rows"]}),
-             "training_variants": sum(len(r["median_us"]) for r in data["rows"]),
-             "fitting": "relative-error least squares with within-shape split contrasts, nonnegative coordinate "
-                        "descent, measured single/multi latency floors (FGW tools/mha/fit_general_split_model.py)"}
-    out = pathlib.Path(args.output)
-    out.write_text(json.dumps(model, indent=1) + "\n", encoding="utf-8")
-    print(json.dumps({"weights": model["weights"], "floors": model["latency_floor_us"],
-                      "calibration": {k: v for k, v in model["validation"]["calibration"].items() if k != "results"},
-                      "leave_one_shape_out": {k: v for k, v in model["validation"]["leave_one_shape_out"].items()
-                                              if k != "results"}}, indent=1))
+    rows = data["rows"]
+    model = {"model": f"b200_general_v{args.version}", "status": "fitted on B200 split sweeps",
+             **fit_and_validate(rows, args.version, args.cores), "hardware": data.get("gpu", "unknown"),
+             "training_sha256": hashlib.sha256(source.read_bytes()).hexdigest(), "training_rows": len(rows),
+             "training_shapes": len({r["case"] for r in rows}),
+             "training_variants": sum(len(r["median_us"]) for r in rows),
+             "fitting": "relative-error least squares plus within-shape ranking (centred rows), exact "
+                        "nonnegative least squares; measured single/multi latency floors"}
+    pathlib.Path(args.output).write_text(json.dumps(model, indent=1) + "\n", encoding="utf-8")
+    brief = {name: {k: v for k, v in model["validation"][name].items() if k != "results"}
+             for name in ("calibration", "leave_one_shape_out")}
+    print(json.dumps({"weights": model["weights"], "floors": model["latency_floor_us"], **brief}, indent=1))
     return 0
 
 

@@ -14,7 +14,7 @@ reproduces the reference bit for bit; the reference's constants 28 and 56 are ``
 ``2 * cores``.
 
 Version 3 is the B200 feature set (no reference counterpart), fitted on B200 split sweeps with the
-reference's method (``fit_split_cost_model.py``) into ``models/b200_general_split_cost_model.json``. It
+reference fitter's loss (``fit_split_cost_model.py``) into ``models/b200_general_split_cost_model.json``. It
 describes the B200 kernels instead of the Ascend ones: query rows per work item are the decode kernel's
 (``decode_rows``) for up to 8 query rows and 256-row pairs above, KV tiles have 128 tokens, serial work
 per program is counted separately for the two kernels, and with one split a tensor-path launch whose items
@@ -168,6 +168,12 @@ def select_model_splits(batch, sq, heads, dim, page_size, width, lengths, model=
     for s in (B200_SPLITS if model["version"] == 3 else SPLITS):
         if s <= capacity_tiles:
             costs[s] = predict_us(batch, sq, heads, dim, lengths, s, model, cores=cores)
+    return pick_within_tolerance(costs, model)
+
+
+def pick_within_tolerance(costs, model):
+    """Smallest split count whose predicted latency is within the model's tolerance of the best prediction
+    (version 1: 2 % relative; later versions: max(2 %, the absolute margin)); ``costs`` maps split -> us."""
     best = min(costs.values())
     tolerance = model["selection_tolerance"]
     if model["version"] == 1:

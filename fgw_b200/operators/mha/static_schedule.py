@@ -21,14 +21,17 @@ plans, so callers and tests written against it run unchanged:
 The device counterpart on B200 is the contiguous schedule of the two-tile kernel (fgw_schedule in
 include/fgw_mha.h): the same balanced cut of ``make_plan`` over (query-tile pair, KV tile) units of every
 request and head, planned on the GPU from the device-resident lengths, with the pieces merged in the same
-launch. ``cores`` defaults to the reference's 28 so its plans (and tests) reproduce; pass the SM count for
-B200-sized plans.
+launch. ``cores`` defaults to the reference's 28 so its plans (and tests) reproduce; any program count up to
+``MAX_CORES`` is accepted (the reference stops at its 28 Ascend cores), so ``make_plan(q, kv, 148)`` is a plan
+for one B200. ``choose_plan`` / ``choose_stream_plan`` search 1..``max_cores`` programs (default 28, the
+reference's search; pass the SM count for B200).
 """
 from dataclasses import dataclass
 from functools import lru_cache
 
 BLOCK = 128  # rows of a Q tile and of a KV block
 REFERENCE_CORES = 28
+MAX_CORES = 4096  # programs a plan may have (one B200 has 148 SMs)
 
 
 @dataclass(frozen=True)
@@ -66,8 +69,8 @@ def _ceil(a, b):
 def _check_shape(q, kv, cores):
     if type(q) is not int or type(kv) is not int or q <= 0 or kv <= 0 or kv % BLOCK:
         raise ValueError("positive integer Q and positive 128-aligned KV required")
-    if type(cores) is not int or not 1 <= cores <= REFERENCE_CORES:
-        raise ValueError("cores must be 1..28")
+    if type(cores) is not int or not 1 <= cores <= MAX_CORES:
+        raise ValueError(f"cores must be 1..{MAX_CORES}")
     tiles, blocks = _ceil(q, BLOCK), kv // BLOCK
     if tiles * blocks > 2**31 - 1:
         raise ValueError("int32 scheduling range exceeded")
@@ -221,10 +224,10 @@ def estimate_cost(plan):
 
 
 @lru_cache(maxsize=128)
-def choose_plan(q, kv):
-    """Cheapest of the whole-Q plan and the balanced plans on 1..28 programs (ties: fewer partials, more
+def choose_plan(q, kv, max_cores=REFERENCE_CORES):
+    """Cheapest of the whole-Q plan and the balanced plans on 1..max_cores programs (ties: fewer partials, more
     programs)."""
-    candidates = [make_q_plan(q, kv)] + [make_plan(q, kv, cores) for cores in range(1, REFERENCE_CORES + 1)]
+    candidates = [make_q_plan(q, kv, max_cores)] + [make_plan(q, kv, cores) for cores in range(1, max_cores + 1)]
     return min(candidates, key=lambda p: (estimate_cost(p)["total_us"], p.partial_count, -len(p.programs)))
 
 
@@ -269,12 +272,12 @@ def make_stream_plan(q, kv, cores=REFERENCE_CORES):
 
 
 @lru_cache(maxsize=128)
-def choose_stream_plan(q, kv):
-    """Best stream or tail plan over 1..28 programs, taken only if it beats whole-Q tiles by more than one
-    block's cost."""
-    direct = make_q_plan(q, kv)
-    candidates = [make_stream_plan(q, kv, cores) for cores in range(1, REFERENCE_CORES + 1)]
-    candidates += [make_tail_plan(q, kv, cores) for cores in range(1, REFERENCE_CORES + 1)]
+def choose_stream_plan(q, kv, max_cores=REFERENCE_CORES):
+    """Best stream or tail plan over 1..max_cores programs, taken only if it beats whole-Q tiles by more than
+    one block's cost."""
+    direct = make_q_plan(q, kv, max_cores)
+    candidates = [make_stream_plan(q, kv, cores) for cores in range(1, max_cores + 1)]
+    candidates += [make_tail_plan(q, kv, cores) for cores in range(1, max_cores + 1)]
     split = min(candidates, key=lambda p: (estimate_cost(p)["total_us"], p.partial_count))
     if estimate_cost(direct)["total_us"] - estimate_cost(split)["total_us"] > COST_MODEL["block_us"]:
         return split

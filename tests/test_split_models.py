@@ -81,8 +81,9 @@ def _sweep():
 
 
 def test_b200_model_is_the_fit_of_the_committed_sweep():
-    # fit_split_cost_model restates FGW's fitter (tools/mha/fit_general_split_model.py); refitting the
-    # committed B200 sweep reproduces the shipped model and its validation
+    # fit_split_cost_model minimises the loss of FGW's fitter (tools/mha/fit_general_split_model.py) by exact
+    # nonnegative least squares; refitting the committed B200 sweep reproduces the shipped model and its
+    # validation
     from fgw_b200.operators.mha.fit_split_cost_model import fit_and_validate
     shipped = gm.load_model(3)
     model = fit_and_validate(_sweep()["rows"], version=3, cores=148)

@@ -116,15 +116,17 @@ def test_grouped_dma_chunk_ownership():
                 assert all(begin % 8 == 0 and 0 < rows <= 8 for worker in workers for *_, begin, rows in worker)
 
 
-def test_b200_sized_plans():
-    # The device's contiguous schedule cuts units the way make_plan does; with 148 programs the reference's
-    # 28-core limit does not apply to the device, so only the cut arithmetic is checked here.
+def test_device_cut_arithmetic():
+    # The device's contiguous schedule cuts units the way make_plan does (program p starts at
+    # p * (T // G) + min(p, T % G)).
     for total, programs in ((4096, 148), (16, 148), (148, 148), (27, 7)):
         starts = [p * (total // programs) + min(p, total % programs) for p in range(programs + 1)]
         loads = [b - a for a, b in zip(starts, starts[1:])]
         assert starts[-1] == total and max(loads) - min(loads) <= 1
-    with pytest.raises(ValueError):
-        make_plan(128, 512, 148)
+    plan = make_plan(4096 * 128, 128, 148)
+    starts = [p * (4096 // 148) + min(p, 4096 % 148) for p in range(149)]
+    assert [sum(seg[2] for seg in program) for program in plan.programs] == \
+        [b - a for a, b in zip(starts, starts[1:])]
 
 
 @pytest.mark.parametrize("maker", [lambda: make_plan(257, 512, 2), lambda: make_tail_plan(257, 512, 2),
@@ -224,3 +226,24 @@ def test_selection_and_merge_tasks_identical_to_reference():
         assert _digest([list(t) for t in make_merge_tasks(plan)]) == golden["make_merge_tasks"][key], key
         assert (_digest([[list(t) for t in w] for w in make_block_merge_tasks(plan)])
                 == golden["make_block_merge_tasks"][key]), key
+
+
+def test_b200_sized_plans_keep_every_invariant():
+    # The planner takes the B200 SM count (the reference stops at its 28 Ascend cores): every plan kind at
+    # 148 programs passes validate_plan (each (Q tile, KV block) exactly once, balanced loads within one block,
+    # consistent slots and merges).
+    for q in (128, 1000, 4096, 8192, 32768):
+        for kv in (512, 2048, 8192, 32768):
+            for make in (make_plan, make_q_plan, make_stream_plan, make_tail_plan):
+                plan = make(q, kv, 148)
+                validate_plan(plan)
+                assert len(plan.programs) <= 148
+    plan = make_plan(8192, 32768, 148)
+    loads = [sum(seg[2] for seg in program) for program in plan.programs]
+    assert len(loads) == 148 and max(loads) - min(loads) <= 1 and sum(loads) == 64 * 256
+    # the search over program counts widens with max_cores; the reference's default stays 1..28
+    assert len(choose_plan(8192, 32768).programs) == 28
+    assert len(choose_plan(8192, 32768, max_cores=148).programs) > 28
+    validate_plan(choose_stream_plan(4096, 2048, max_cores=148))
+    with pytest.raises(ValueError):
+        make_plan(128, 512, 0)
