@@ -47,6 +47,7 @@ EXPORTED = (
     "fgw_mha_merge",
     "fgw_mha_read_error",
     "fgw_mha_paged_fwd_static_ws",
+    "fgw_mha_static_ws_read_error",
     "fgw_mha_selftest_wait",
     "fgw_paged_cache_gather",
 )
@@ -161,6 +162,8 @@ def library():
     lib.fgw_mha_selftest_wait.restype = ctypes.c_int
     lib.fgw_mha_paged_fwd_static_ws.argtypes = [p, vp]
     lib.fgw_mha_paged_fwd_static_ws.restype = ctypes.c_int
+    lib.fgw_mha_static_ws_read_error.argtypes = [vp, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int)]
+    lib.fgw_mha_static_ws_read_error.restype = ctypes.c_int
     lib.fgw_paged_cache_gather.argtypes = [ctypes.POINTER(GatherParams), vp]
     lib.fgw_paged_cache_gather.restype = ctypes.c_int
     _LIB = lib
@@ -243,6 +246,15 @@ def selftest_wait(workspace_ptr, workspace_bytes, budget_ms, complete, stream_pt
 def paged_fwd_static_ws(params, stream_ptr):
     """Forward with the library's own static scratch array: allocates nothing (see include/fgw_mha.h)."""
     check(library().fgw_mha_paged_fwd_static_ws(ctypes.byref(params), stream_ptr), "fgw_mha_paged_fwd_static_ws")
+
+
+def static_ws_read_error(stream_ptr):
+    """(device_status, site) of the last static-workspace forward on the current device; synchronises."""
+    status = ctypes.c_int(0)
+    site = ctypes.c_int(0)
+    check(library().fgw_mha_static_ws_read_error(stream_ptr, ctypes.byref(status), ctypes.byref(site)),
+          "fgw_mha_static_ws_read_error")
+    return status.value, site.value
 
 
 def paged_cache_gather(params, stream_ptr):

@@ -42,6 +42,23 @@ int static_workspace_ptr(void** ptr) {
 
 }  // namespace
 
+// Status of the last fgw_mha_paged_fwd_static_ws call on the current device: the workspace header lives in the
+// library's array, so the caller (who never sees its address) reads it here. Copies the header's two words out
+// of the array by symbol; allocates nothing.
+extern "C" int fgw_mha_static_ws_read_error(void* stream, int* device_status, int* site) {
+  if (device_status == nullptr) return FGW_ERR_INVALID_ARGUMENT;
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess) return FGW_ERR_NO_DEVICE;
+  if (cudaStreamSynchronize(static_cast<cudaStream_t>(stream)) != cudaSuccess) return FGW_ERR_CUDA;
+  int32_t words[2] = {0, 0};
+  if (cudaMemcpyFromSymbol(words, g_static_workspace, sizeof(words), 0, cudaMemcpyDeviceToHost) != cudaSuccess) {
+    return FGW_ERR_CUDA;
+  }
+  *device_status = words[0];
+  if (site != nullptr) *site = words[1];
+  return FGW_OK;
+}
+
 extern "C" int fgw_mha_paged_fwd_static_ws(const fgw_mha_params* params, void* stream) {
   if (params == nullptr) return FGW_ERR_INVALID_ARGUMENT;
   fgw_mha_params p = *params;

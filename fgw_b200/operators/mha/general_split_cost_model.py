@@ -46,6 +46,7 @@ FEATURE_NAMES_V3 = (
 DECODE_MAX_QUERIES = 8  # query rows per request at or below which the decode kernel runs
 PAIR_ROWS = 256         # query rows per tensor-path work item (two 128-row tiles)
 KV_TILE = 128
+STREAM_MAX_PROGRAMS = 148  # programs of the contiguous schedule at most (kStreamMaxPrograms in the library)
 
 
 def model_path(version=1):
@@ -76,8 +77,8 @@ def _features_b200(batch, sq, heads, dim, lengths, splits, cores):
     rows = decode_rows(dim) if decode else PAIR_ROWS
     items = batch * heads * ((sq + rows - 1) // rows) * splits
     pieces = 0.0
-    if not decode and splits == 1 and 3 * items < 2 * min(cores, 148):
-        programs = min(cores, 148)
+    if not decode and splits == 1 and 3 * items < 2 * STREAM_MAX_PROGRAMS:
+        programs = min(cores, STREAM_MAX_PROGRAMS)
         serial = math.ceil(items * max(mean_tiles, 1.0) / programs)
         waves = 1
         # an item cut into this many pieces is merged by one CTA (it reads every other piece's partial rows)

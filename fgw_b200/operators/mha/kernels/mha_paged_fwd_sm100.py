@@ -79,9 +79,7 @@ def _dtype_code(dtype):
     return _native.DTYPE_BFLOAT16 if str(dtype) in ("bfloat16", "torch.bfloat16") else _native.DTYPE_FLOAT16
 
 
-def _b200_model(name):
-    if name == "v7":
-        return v7_model.load_model(v7_model.B200_MODEL)
+def _b200_model():
     return general_model.load_model(3)  # the B200 feature set fitted on B200 split sweeps
 
 
@@ -90,7 +88,7 @@ def _select_auto_splits(batch, sq, heads, dim, width, page_size, lengths, cores)
     if lengths is None:
         lengths = (width * page_size,) * batch
     return general_model.select_model_splits(batch, sq, heads, dim, page_size, width, list(lengths),
-                                             model=_b200_model("general"), cores=cores)
+                                             model=_b200_model(), cores=cores)
 
 
 @functools.lru_cache(maxsize=128)
@@ -158,7 +156,7 @@ def build_kernel(batch, sq, heads, dim, pool_rows, width, page_size, causal, dty
             if cache_lengths is None:
                 raise ValueError("Experimental cost model requires host-known cache_lengths")
             splits = general_model.select_model_splits(batch, sq, heads, dim, page_size, width, list(cache_lengths),
-                                                       model=_b200_model("general"), cores=cores)
+                                                       model=_b200_model(), cores=cores)
             policy_name = "cost_model"
         elif num_splits is None and split_policy == "auto":
             # The reference's rule here fills the cores (fill_28); over 148 SMs that over-splits (the config-3

@@ -5,8 +5,8 @@ a non-negative linear score, argmin with ties going to the smaller split (:13-31
 promotion guard ``eligible_config`` (:34-44). With the reference coefficients
 (``models/reference_split_cost_model.json``) and ``cores=28`` every selection is bit-identical
 to the reference's; ``tests/test_split_models.py`` checks that against tables generated from the
-reference itself. On B200 the same features run with ``cores`` = the SM count (148) and the
-B200 coefficients of ``models/b200_split_cost_model.json``.
+reference itself. The B200 routes choose their split counts with the version-3 model of
+``general_split_cost_model`` instead; this selector is kept for the reference's ``cost_model`` parity.
 """
 import functools
 import json
@@ -15,7 +15,6 @@ import pathlib
 SPLITS = (1, 2, 4, 8, 16)
 MODEL_DIR = pathlib.Path(__file__).with_name("models")
 REFERENCE_MODEL = MODEL_DIR / "reference_split_cost_model.json"
-B200_MODEL = MODEL_DIR / "b200_split_cost_model.json"
 
 
 @functools.lru_cache(maxsize=8)

@@ -182,6 +182,12 @@ FGW_API int fgw_mha_merge(const fgw_mha_params* params, void* workspace, size_t 
  * serialise them. */
 FGW_API int fgw_mha_paged_fwd_static_ws(const fgw_mha_params* params, void* stream);
 
+/* Device-side status of fgw_mha_paged_fwd_static_ws calls on the current device, for callers that never see
+ * the library array's address (no reference counterpart): synchronises `stream`, then reports the error word
+ * and wait site of the array's workspace header like fgw_mha_read_error. Each static-workspace call clears
+ * them first, so the status is that of the last call. Allocates nothing. */
+FGW_API int fgw_mha_static_ws_read_error(void* stream, int* device_status, int* site);
+
 /* Synchronises `stream`, then reports the device-side status recorded in the workspace header
  * (FGW_OK or FGW_ERR_DEVICE_TIMEOUT) and which wait site gave up (0 when clean). */
 FGW_API int fgw_mha_read_error(const void* workspace, void* stream, int* device_status, int* site);

@@ -54,6 +54,8 @@ def test_static_workspace_matches_regular_entry_point_twice(case, path, splits, 
         rtol, atol = TOLERANCE[dtype_name(torch.bfloat16)]
         torch.testing.assert_close(got, expected, rtol=rtol, atol=atol, msg=f"call {call}")
         assert (got.float() - expected.float()).abs().max().item() <= MAX_ABS["bfloat16"]
+        # the device-side status lives in the library's array; this entry point reads it back
+        assert _native.static_ws_read_error(stream) == (_native.OK, 0)
 
 
 def test_static_workspace_rejects_requests_beyond_its_size():
