@@ -521,21 +521,44 @@ def run_gather(args, dc, device, stream):
             "packed_rows": offsets[-1], "launches": (len(fns) + len(afns)) * steps}
 
 
-def cpu_threads():
+def host_cores():
+    """Physical cores of this host (logical CPUs when the count of physical ones is unknown)."""
     try:
-        from threadpoolctl import threadpool_info
-        info = threadpool_info()
-        counts = [i.get("num_threads", 1) for i in info if i.get("internal_api") in ("openblas", "mkl", "blis")]
+        import psutil
+        count = psutil.cpu_count(logical=False)
+    except Exception:
+        count = None
+    return count or os.cpu_count() or 1
+
+
+def use_all_host_cores():
+    """Lets NumPy's BLAS use every physical core, whatever OMP_NUM_THREADS torchrun set (it sets 1), and
+    returns the thread count the BLAS pools now have."""
+    cores = host_cores()
+    try:
+        from threadpoolctl import threadpool_info, threadpool_limits
+        threadpool_limits(limits=cores, user_api="blas")
+        counts = [i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"]
         if counts:
             return max(counts)
     except Exception:
         pass
-    return os.cpu_count() or 1
+    return cores
+
+
+def headline_config(world):
+    """Workload description of the headline line, shared by both arms so the driver can match them."""
+    c = LONGQ
+    return {"workload": "longq_b2h8_q4096_kv2048_bf16_d128_page128", "global_batch": c["batch"] * world,
+            "seq_len": c["sq"], "kv_len": c["kv"], "heads": c["heads"], "head_dim": c["dim"], "page": c["page"],
+            "parallelism": f"batch-shard x{world}",
+            "l2": "flushed (256 MiB write) before every timed step"}
 
 
 def cpu_longq_sample(budget_s=12.0):
     """Times the NumPy oracle on the headline workload, growing the sample until ~budget_s of work."""
     from oracle import paged_attention_chunked, useful_flops
+    cores = use_all_host_cores()
     c = LONGQ
     width = c["kv"] // c["page"]
     rng = np.random.default_rng(5)
@@ -561,7 +584,7 @@ def cpu_longq_sample(budget_s=12.0):
             elif heads < c["heads"]:
                 heads *= 2
     value = flops / elapsed / 1e12
-    return {"value": value, "unit": "TFLOP/s", "cores": cpu_threads(), "kind": "port",
+    return {"value": value, "unit": "TFLOP/s", "cores": cores, "kind": "port",
             "sample": f"{calls} oracle calls on slices of config 2 (last: 1 request, {rows} query rows, {heads} heads,"
                       f" KV 2048), {elapsed:.1f} s of CPU work, NumPy FP32 restatement of FGW's reference()"}
 
@@ -650,6 +673,7 @@ def reference_arm(args, rank, world):
     if rank != 0:
         return 0
     from oracle import paged_attention_chunked, useful_flops
+    cores = use_all_host_cores()
     c = LONGQ
     width = c["kv"] // c["page"]
     rng = np.random.default_rng(5)
@@ -679,13 +703,12 @@ def reference_arm(args, rank, world):
     ms = 1e3 * sum(times) / len(times)
     value = flops / (ms * 1e-3) / 1e12
     sample = (f"{rows} of 4096 query rows per request (B2 H8 KV2048 D128), FP32 NumPy restatement of FGW's CPU "
-              "reference, all host BLAS threads")
+              f"reference, BLAS on {cores} threads (every physical core of the host)")
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "longq_b2h8_q4096_kv2048_bf16_d128_page128", "global_batch": LONGQ["batch"],
-                       "seq_len": LONGQ["sq"], "kv_len": LONGQ["kv"], "parallelism": "host"},
-            "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": cpu_threads(), "kind": "port",
+            "config": headline_config(world),
+            "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": cores, "kind": "port",
                              "sample": sample},
             "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -733,12 +756,10 @@ def main(argv=None):
             "value": total_flops / (step_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": step_ms,
             "us_per_call": step_ms * 1e3,
             "vs_baseline": (total_flops / (step_ms * 1e-3) / 1e12 / world) / ASCEND_V7_TFLOPS,
-            "config": {"workload": "longq_b2h8_q4096_kv2048_bf16_d128_page128", "global_batch": c["batch"] * world,
-                       "seq_len": c["sq"], "kv_len": c["kv"], "parallelism": f"batch-shard x{world}",
-                       "l2": "flushed (256 MiB write) before every timed step", "num_splits": k.num_splits,
-                       "execution_path": k.execution_path, "compute_grid": k.compute_grid,
-                       "vs_baseline_source": "published: 237.4 TFLOP/s, FGW v7 persistent28 on Ascend 950PR "
-                                             "(per GPU)"},
+            "config": headline_config(world),
+            "kernel": {"num_splits": k.num_splits, "execution_path": k.execution_path,
+                       "compute_grid": k.compute_grid, "task_assignment": k.task_assignment},
+            "vs_baseline_source": "published: 237.4 TFLOP/s, FGW v7 persistent28 on Ascend 950PR (per GPU)",
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": tc_peak, "unit": "TFLOP/s",
                          "frac": achieved / tc_peak, "traffic": traffic,
                          "kernel": "attend (" + k.execution_path + ")", "peak_source": f"{peak_kind} bf16_tflops"},

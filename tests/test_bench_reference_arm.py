@@ -24,9 +24,10 @@ def test_reference_arm_prints_the_contract_line():
     assert d["impl"] == "reference" and d["metric"] == bench.METRIC and d["unit"] == "TFLOP/s"
     assert d["value"] > 0 and d["ms_per_step"] > 0 and d["steps"] == 1 and d["warmup"] == 0
     assert d["higher_is_better"] is True and d["vs_baseline"] is None
-    assert d["config"]["workload"] == "longq_b2h8_q4096_kv2048_bf16_d128_page128"
+    assert d["config"] == bench.headline_config(1)  # the repo arm's config, key for key
     base = d["cpu_baseline"]
-    assert base["value"] == d["value"] and base["kind"] == "port" and base["cores"] >= 1 and base["sample"]
+    assert base["value"] == d["value"] and base["kind"] == "port" and base["sample"]
+    assert base["cores"] == bench.host_cores()  # every physical core, whatever OMP_NUM_THREADS says
     assert d["e2e"] == {"value": d["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
 
 
@@ -36,3 +37,11 @@ def test_reference_arm_on_other_ranks_does_no_work():
     with contextlib.redirect_stdout(out):
         assert bench.reference_arm(args, 1, 2) == 0
     assert out.getvalue() == ""
+
+
+def test_reference_arm_uses_every_core_under_torchrun_settings(monkeypatch):
+    # torchrun exports OMP_NUM_THREADS=1; the arm raises the BLAS pools back to the host's physical cores
+    from threadpoolctl import threadpool_info, threadpool_limits
+    with threadpool_limits(limits=1, user_api="blas"):
+        assert bench.use_all_host_cores() == bench.host_cores()
+        assert max(i["num_threads"] for i in threadpool_info() if i["user_api"] == "blas") == bench.host_cores()
