@@ -32,13 +32,20 @@ SCHEDULE_STRIDED = 1
 SCHEDULE_CONTIGUOUS = 2
 SCHEDULE_TAIL = 3
 
-ABI_VERSION = 3  # FGW_MHA_ABI_VERSION the Params / GatherParams layouts below match
+# fgw_tensor_kernel
+TENSOR_KERNEL_AUTO = 0
+TENSOR_KERNEL_PAIRS = 1
+TENSOR_KERNEL_SINGLE = 2
+TENSOR_KERNEL_HALVES = 3
+
+ABI_VERSION = 4  # FGW_MHA_ABI_VERSION the Params / GatherParams layouts below match
 
 EXPORTED = (
     "fgw_mha_abi_version",
     "fgw_mha_status_string",
     "fgw_mha_device_sm_count",
     "fgw_mha_resolve_path",
+    "fgw_mha_resolve_schedule",
     "fgw_mha_workspace_size",
     "fgw_mha_paged_fwd",
     "fgw_mha_plan",
@@ -91,7 +98,8 @@ class Params(ctypes.Structure):
         ("path", ctypes.c_int32),
         ("wait_budget_ms", ctypes.c_int32),
         ("schedule", ctypes.c_int32),
-        ("reserved", ctypes.c_int32 * 3),
+        ("tensor_kernel", ctypes.c_int32),
+        ("reserved", ctypes.c_int32 * 2),
     ]
 
 
@@ -150,6 +158,8 @@ def library():
     lib.fgw_mha_device_sm_count.restype = ctypes.c_int
     lib.fgw_mha_resolve_path.argtypes = [p, ctypes.POINTER(ctypes.c_int)]
     lib.fgw_mha_resolve_path.restype = ctypes.c_int
+    lib.fgw_mha_resolve_schedule.argtypes = [p, ctypes.POINTER(ctypes.c_int)]
+    lib.fgw_mha_resolve_schedule.restype = ctypes.c_int
     lib.fgw_mha_workspace_size.argtypes = [p, ctypes.POINTER(ctypes.c_size_t)]
     lib.fgw_mha_workspace_size.restype = ctypes.c_int
     for name in ("fgw_mha_paged_fwd", "fgw_mha_plan", "fgw_mha_attend", "fgw_mha_partial", "fgw_mha_merge"):
@@ -195,6 +205,13 @@ def device_sm_count(device):
 def resolve_path(params):
     out = ctypes.c_int(0)
     check(library().fgw_mha_resolve_path(ctypes.byref(params), ctypes.byref(out)), "fgw_mha_resolve_path")
+    return out.value
+
+
+def resolve_schedule(params):
+    """The schedule (SCHEDULE_STRIDED / _CONTIGUOUS / _TAIL) the main launch takes for ``params``."""
+    out = ctypes.c_int(0)
+    check(library().fgw_mha_resolve_schedule(ctypes.byref(params), ctypes.byref(out)), "fgw_mha_resolve_schedule")
     return out.value
 
 

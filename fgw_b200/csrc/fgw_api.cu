@@ -30,36 +30,41 @@ EncodeTiledFn encode_tiled() {
   return fn;
 }
 
-// FGW_MHA_TENSOR_SINGLE_TILE=1 selects the one-query-tile tensor kernel for every head dimension
-// (the two-tile kernel is the default for head_dim <= 128); read once per process.
-static bool single_tile_requested() {
-  static const bool value = [] {
-    const char* v = std::getenv("FGW_MHA_TENSOR_SINGLE_TILE");
-    return v != nullptr && v[0] == '1';
-  }();
-  return value;
-}
-
-// Opt-in key-halves tensor kernel (fgw_fmha_halves_sm100.cu): FGW_MHA_TENSOR_KERNEL=halves.
-static bool key_halves_requested() {
-  static const bool value = [] {
-    const char* v = std::getenv("FGW_MHA_TENSOR_KERNEL");
-    return v != nullptr && std::strcmp(v, "halves") == 0;
-  }();
-  return value;
+// The tcgen05 kernel the tensor path runs for these parameters (FGW_TENSOR_KERNEL_AUTO resolved).
+int resolve_tensor_kernel(const fgw_mha_params& p) {
+  if (p.tensor_kernel != FGW_TENSOR_KERNEL_AUTO) return p.tensor_kernel;
+  return p.head_dim <= 128 ? FGW_TENSOR_KERNEL_PAIRS : FGW_TENSOR_KERNEL_SINGLE;
 }
 
 long long pair_items(const fgw_mha_params& p) {
   return static_cast<long long>(p.batch) * p.heads * p.num_splits * ((p.q_len + kPairRows - 1) / kPairRows);
 }
 
-// AUTO takes the contiguous schedule only when whole items would leave more than a third of the programs
-// idle in their single wave (items < 2/3 of the programs): measured on config 2 (256 items, 148 programs,
-// two waves) the strided schedule is faster, since cutting items adds segment starts and piece merges.
+long long stream_items(const fgw_mha_params& p) {
+  if (resolve_path(p) == FGW_PATH_DECODE) {
+    const int rows = decode_rows_per_item(p.head_dim);
+    return static_cast<long long>(p.batch) * ((p.q_len + rows - 1) / rows) * p.heads * p.num_splits;
+  }
+  return pair_items(p);
+}
+
+int stream_slot_rows(const fgw_mha_params& p) {
+  return resolve_path(p) == FGW_PATH_DECODE ? decode_rows_per_item(p.head_dim) : kPairRows;
+}
+
+// Decode path, one split: the contiguous schedule unless STRIDED is asked for. Its cut gives every CTA the same
+// number of KV stages whatever the spread of cache lengths (whole items dealt round-robin leave the CTAs that
+// drew the longest requests as stragglers when there are few items per CTA), and costs two piece partials per
+// CTA at most.
+// Tensor path: AUTO takes the contiguous schedule only when whole items would leave more than a third of the
+// programs idle in their single wave (items < 2/3 of the programs): measured on config 2 (256 items, 148
+// programs, two waves) the strided schedule is faster, since cutting items adds segment starts and piece
+// merges.
 bool use_stream_schedule(const fgw_mha_params& p) {
-  if (p.schedule == FGW_SCHEDULE_STRIDED) return false;
-  const bool applies = resolve_path(p) == FGW_PATH_TENSOR && p.head_dim <= 128 && p.num_splits == 1 &&
-                       !single_tile_requested() && !key_halves_requested() && pair_items(p) <= kStreamMaxItems;
+  if (p.schedule == FGW_SCHEDULE_STRIDED || p.num_splits != 1) return false;
+  if (stream_items(p) > kStreamMaxItems) return false;
+  if (resolve_path(p) == FGW_PATH_DECODE) return true;
+  const bool applies = p.head_dim <= 128 && resolve_tensor_kernel(p) == FGW_TENSOR_KERNEL_PAIRS;
   if (!applies) return false;
   return p.schedule == FGW_SCHEDULE_CONTIGUOUS || p.schedule == FGW_SCHEDULE_TAIL ||
          3 * pair_items(p) < 2ll * kStreamMaxPrograms;
@@ -74,15 +79,16 @@ struct StreamSizes {
 
 StreamSizes stream_sizes(const fgw_mha_params& p) {
   const size_t programs = kStreamMaxPrograms;
-  const size_t items = static_cast<size_t>(pair_items(p));
+  const size_t items = static_cast<size_t>(stream_items(p));
+  const size_t rows = static_cast<size_t>(stream_slot_rows(p));
   StreamSizes z;
   z.prog_item = align256(programs * sizeof(int32_t));
   z.prog_off = align256(programs * sizeof(int32_t));
   z.prog_u = align256((programs + 1) * sizeof(long long));
   z.prefix = align256((items + 1) * sizeof(long long));
   z.counters = align256(items * sizeof(int32_t));
-  z.slot_lse = align256(2 * programs * kPairRows * sizeof(float));
-  z.slot_o = align256(2 * programs * kPairRows * static_cast<size_t>(p.head_dim) * sizeof(float));
+  z.slot_lse = align256(2 * programs * rows * sizeof(float));
+  z.slot_o = align256(2 * programs * rows * static_cast<size_t>(p.head_dim) * sizeof(float));
   return z;
 }
 }  // namespace
@@ -126,7 +132,8 @@ void carve_workspace(LaunchDesc& d, void* workspace, int path) {
   d.contiguous = use_stream_schedule(p);
   if (d.contiguous) {
     const StreamSizes z = stream_sizes(p);
-    d.items = static_cast<int>(pair_items(p));
+    d.items = static_cast<int>(stream_items(p));
+    d.slot_rows = stream_slot_rows(p);
     d.prog_item = reinterpret_cast<int32_t*>(base);
     base += z.prog_item;
     d.prog_off = reinterpret_cast<int32_t*>(base);
@@ -171,7 +178,10 @@ static int validate(const fgw_mha_params* p) {
   if (p->grid_cap < 0 || p->wait_budget_ms < 0) return FGW_ERR_INVALID_ARGUMENT;
   if (p->path < FGW_PATH_AUTO || p->path > FGW_PATH_TENSOR) return FGW_ERR_INVALID_ARGUMENT;
   if (p->schedule < FGW_SCHEDULE_AUTO || p->schedule > FGW_SCHEDULE_TAIL) return FGW_ERR_INVALID_ARGUMENT;
-  for (int i = 0; i < 3; ++i) {
+  if (p->tensor_kernel < FGW_TENSOR_KERNEL_AUTO || p->tensor_kernel > FGW_TENSOR_KERNEL_HALVES) {
+    return FGW_ERR_INVALID_ARGUMENT;
+  }
+  for (int i = 0; i < 2; ++i) {
     if (p->reserved[i] != 0) return FGW_ERR_INVALID_ARGUMENT;
   }
   if (!p->q || !p->k_cache || !p->v_cache || !p->block_table || !p->cache_seqlens || !p->out) {
@@ -217,8 +227,7 @@ static int prepare(const fgw_mha_params* params, void* workspace, size_t workspa
   const int budget_ms = d.p.wait_budget_ms > 0 ? d.p.wait_budget_ms : 2000;
   d.budget_ns = static_cast<uint64_t>(budget_ms) * 1000000ull;
   d.stream = static_cast<cudaStream_t>(stream);
-  d.single_tile = single_tile_requested();
-  d.key_halves = key_halves_requested() && !d.single_tile;
+  d.tensor_kernel = resolve_tensor_kernel(d.p);
   if (d.contiguous) {
     const int cap = d.p.grid_cap > 0 ? d.p.grid_cap : d.sm_count;
     d.programs = std::min(std::min(cap, d.sm_count), kStreamMaxPrograms);
@@ -273,6 +282,16 @@ int fgw_mha_device_sm_count(int device, int* sm_count) {
 int fgw_mha_resolve_path(const fgw_mha_params* params, int* path) {
   if (params == nullptr || path == nullptr) return FGW_ERR_INVALID_ARGUMENT;
   *path = resolve_path(*params);
+  return FGW_OK;
+}
+
+int fgw_mha_resolve_schedule(const fgw_mha_params* params, int* schedule) {
+  if (params == nullptr || schedule == nullptr) return FGW_ERR_INVALID_ARGUMENT;
+  if (!use_stream_schedule(*params)) {
+    *schedule = FGW_SCHEDULE_STRIDED;
+  } else {
+    *schedule = params->schedule == FGW_SCHEDULE_TAIL ? FGW_SCHEDULE_TAIL : FGW_SCHEDULE_CONTIGUOUS;
+  }
   return FGW_OK;
 }
 

@@ -5,8 +5,8 @@
 //   round-robin start with the longest requests (longest-processing-time-first). This is the
 //   length-aware part of the reference's persistent scheduler (v7.py:112-113, 260-270), moved
 //   onto the device so no length ever has to cross to the host.
-//   With the contiguous schedule it also lays the two-tile kernel's work items end to end and cuts
-//   them into one equal range of KV tiles per program (StreamPlanArgs below).
+//   With the contiguous schedule it also lays the work items (the two-tile kernel's, or the decode kernel's)
+//   end to end and cuts them into one equal range of KV units per program (StreamPlanArgs below).
 // merge_kernel: LSE-weighted merge of split-KV partials, one warp per output row; replaces the
 //   reference merge prim_funcs (v7.py:317-371, cube_general.py:224-279). Partials carry a base-2
 //   LSE; the empty-split sentinel and validity threshold keep the reference's -1e30 / -1e29. The
@@ -25,6 +25,9 @@ constexpr int kPlanSortMax = 8192;
 // reference's balanced plan (static_schedule.py:64-66).
 struct StreamPlanArgs {
   int enabled, items, programs, heads, sq, causal, qpairs;
+  // decode path (decode != 0): items are (request, query-row block, head) with `rows` query rows each and
+  // `tile`-token KV units (the decode kernel's stage), `row_blocks` blocks per request
+  int decode, rows, tile, row_blocks;
   int first;  // first item of the cut range (0, or the items of the full waves under the tail schedule)
   int32_t* prog_item;
   int32_t* prog_off;
@@ -37,6 +40,15 @@ struct StreamPlanArgs {
 // item decomposition with one split (pair_item in fgw_fmha2_sm100.cu).
 __device__ __forceinline__ long long stream_item_units(const StreamPlanArgs& s, const int32_t* lens,
                                                        const int32_t* order, int item) {
+  if (s.decode) {
+    // decode_item in fgw_decode.cu with one split: heads innermost, then the query-row block
+    const int rest = item / s.heads;
+    const int rb = rest % s.row_blocks;
+    const int len = lens[order[rest / s.row_blocks]];
+    const int last = min(rb * s.rows + s.rows, s.sq) - 1;
+    const int visible = s.causal ? max(len - s.sq + last + 1, 0) : len;
+    return max((visible + s.tile - 1) / s.tile, 1);
+  }
   const int p_rev = item % s.qpairs;
   const int b = order[(item / s.qpairs) / s.heads];
   const int q0 = (s.qpairs - 1 - p_rev) * 256;
@@ -172,6 +184,12 @@ cudaError_t launch_plan(const LaunchDesc& d) {
     sp.sq = d.p.q_len;
     sp.causal = d.p.causal;
     sp.qpairs = (d.p.q_len + kPairRows - 1) / kPairRows;
+    if (resolve_path(d.p) == FGW_PATH_DECODE) {
+      sp.decode = 1;
+      sp.rows = decode_rows_per_item(d.p.head_dim);
+      sp.tile = decode_tile_tokens(d.p.head_dim);
+      sp.row_blocks = (d.p.q_len + sp.rows - 1) / sp.rows;
+    }
     sp.prog_item = d.prog_item;
     sp.prog_off = d.prog_off;
     sp.prog_u = d.prog_u;

@@ -285,6 +285,28 @@ __device__ __forceinline__ float merge_split_finish(float acc, float total) {
 }
 
 // ---------------------------------------------------------------------------------------
+// Contiguous schedule: T units cut into G programs; program p owns units [start(p), start(p + 1)),
+// start(p) = p (T / G) + min(p, T % G) (the reference's balanced plan, static_schedule.py:64-66). An item cut
+// between programs q_first .. q_first + pieces - 1 leaves one partial per piece in two slots per program:
+// slot 2 q for the piece a program starts with, 2 q + 1 for the one it ends with.
+// ---------------------------------------------------------------------------------------
+__device__ __forceinline__ long long program_start(long long total, int programs, int p) {
+  return static_cast<long long>(p) * (total / programs) + min(static_cast<long long>(p), total % programs);
+}
+
+__device__ __forceinline__ int program_of(long long total, int programs, long long u) {
+  const long long b = total / programs, r = total % programs;
+  if (u < r * (b + 1)) return static_cast<int>(u / (b + 1));
+  return static_cast<int>(r + (u - r * (b + 1)) / b);
+}
+
+// Slot of piece k of an item whose first piece is held by program q_first; first_extra = 1 when the item
+// starts inside q_first's range (that piece is q_first's last piece), 0 when it starts at the range's start.
+__device__ __forceinline__ long long piece_slot(int q_first, int first_extra, int k) {
+  return 2ll * q_first + first_extra + (k == 0 ? 0 : 2 * k - first_extra);
+}
+
+// ---------------------------------------------------------------------------------------
 // tcgen05: TMEM allocation, UMMA issue/commit, TMEM loads and stores
 // ---------------------------------------------------------------------------------------
 __device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {

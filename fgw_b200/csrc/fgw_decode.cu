@@ -2,8 +2,10 @@
 //
 // Replaces the reference's SIMT split-KV kernels (operators/mha/kernels/mha_paged_decode_ascend_v2.py:34-129,
 // v1 for one split) and the Q~1 use of the v7 Cube kernel. Design for B200:
-//   * one persistent CTA per SM walks a static round-robin list of work items
-//     (request, query-row block, split, head) in descending-cache-length order (LPT);
+//   * one persistent CTA per SM walks its share of the work items (request, query-row block, split, head),
+//     requests in descending-cache-length order (LPT): with one split the items' KV stages, laid end to end,
+//     are cut into one equal range per CTA (contiguous schedule; an item cut between CTAs is merged in place by
+//     the CTA completing it), otherwise whole items are dealt round-robin;
 //   * a producer warp streams each item's live KV pages into a shared-memory ring with TMA,
 //     one 3-D box {head_dim, 1, rows} per (page slice, K or V), driven by the block table;
 //   * eight consumer warps split a tile's tokens into groups of LPT lanes; each group owns
@@ -33,6 +35,15 @@ struct DecodeArgs {
   // fused split merge: arrivals per (request, row block, head) group; the CTA completing a group merges it
   int fused_merge;
   int32_t* merge_counters;
+  // contiguous schedule (one split): per-program first item, unit offset and first unit, the per-item arrival
+  // counters and the two partial slots of every program (kRows rows each); whole items below tail_start first
+  int contiguous, programs, tail_start;
+  const int32_t* prog_item;
+  const int32_t* prog_off;
+  const long long* prog_u;
+  int32_t* counters;
+  float* slot_lse;
+  float* slot_o;
   long long items;
   float scale_log2;
   uint64_t budget_ns;
@@ -73,6 +84,88 @@ __device__ __forceinline__ void decode_item(long long item, int heads, int split
   b = order[rest / row_blocks];
 }
 
+// One run of KV stages of one work item processed by this CTA: a whole item (its split's range), or, with the
+// contiguous schedule, units [first, first + count) of an item, which is a piece when other CTAs hold the rest.
+struct DecodeSegment {
+  long long item;
+  int first, count;  // count < 0: whole item, the split's range of stages
+  bool piece;
+  long long item_u;  // first unit of the item in the contiguous cut
+  int units;         // units of the whole item (at least 1)
+};
+
+struct DecodeCursor {
+  long long whole;  // next whole item (strided part)
+  long long item;
+  int off;
+  long long u, u_end;
+};
+
+// KV units of a decode item (stages seen by its last query row, at least 1): the plan's stream_item_units.
+template <int D>
+__device__ __forceinline__ int decode_units(const DecodeArgs& a, long long item) {
+  using S = DecodeShape<D>;
+  int b, rb, s, h;
+  decode_item(item, a.heads, a.splits, a.row_blocks, a.order, b, rb, s, h);
+  const int len = a.lengths[b];
+  const int last = min(rb * S::kRows + S::kRows, a.sq) - 1;
+  const int visible = a.causal ? max(len - a.sq + last + 1, 0) : len;
+  return max((visible + S::kTile - 1) / S::kTile, 1);
+}
+
+__device__ __forceinline__ void decode_cursor_init(const DecodeArgs& a, DecodeCursor& k) {
+  k.whole = blockIdx.x;
+  k.item = a.contiguous ? a.prog_item[blockIdx.x] : 0;
+  k.off = a.contiguous ? a.prog_off[blockIdx.x] : 0;
+  k.u = a.contiguous ? a.prog_u[blockIdx.x] : 0;
+  k.u_end = a.contiguous ? a.prog_u[blockIdx.x + 1] : 0;
+}
+
+// The producer and the consumers walk the same segments in the same order: whole items first (all of them
+// with the strided schedule), then the CTA's contiguous range of units.
+template <int D>
+__device__ __forceinline__ bool decode_next(const DecodeArgs& a, DecodeCursor& k, DecodeSegment& sg) {
+  const long long whole_end = a.contiguous ? a.tail_start : a.items;
+  if (k.whole < whole_end) {
+    sg.item = k.whole;
+    sg.first = 0;
+    sg.count = -1;
+    sg.piece = false;
+    sg.item_u = 0;
+    sg.units = 0;
+    k.whole += gridDim.x;
+    return true;
+  }
+  if (!a.contiguous || k.u >= k.u_end) return false;
+  const int units = decode_units<D>(a, k.item);
+  const int count = static_cast<int>(min(static_cast<long long>(units - k.off), k.u_end - k.u));
+  sg.item = k.item;
+  sg.first = k.off;
+  sg.count = count;
+  sg.piece = count < units;
+  sg.item_u = k.u - k.off;
+  sg.units = units;
+  k.u += count;
+  k.off += count;
+  if (k.off >= units) {
+    ++k.item;
+    k.off = 0;
+  }
+  return true;
+}
+
+// Stages [t_begin, t_end) of a segment over an item with `tiles` stages.
+__device__ __forceinline__ void segment_range(const DecodeSegment& sg, int tiles, int s, int splits, int& t_begin,
+                                              int& t_end) {
+  if (sg.count < 0) {
+    t_begin = static_cast<int>((long long)tiles * s / splits);
+    t_end = static_cast<int>((long long)tiles * (s + 1) / splits);
+  } else {
+    t_begin = min(sg.first, tiles);
+    t_end = min(sg.first + sg.count, tiles);
+  }
+}
+
 template <typename T, int D>
 __global__ void __launch_bounds__(DecodeShape<D>::kThreads, 1)
     decode_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
@@ -101,7 +194,6 @@ __global__ void __launch_bounds__(DecodeShape<D>::kThreads, 1)
   }
   __syncthreads();
 
-  const int grid = gridDim.x;
   if (warp == S::kWarps) {
     // ----------------------------------------------------------------- producer warp
     if (lane == 0) {
@@ -112,15 +204,18 @@ __global__ void __launch_bounds__(DecodeShape<D>::kThreads, 1)
       uint32_t it = 0;
       const int boxes = S::kTile / a.box_rows;
       const uint32_t box_bytes = a.box_rows * D * sizeof(T);
-      for (long long item = blockIdx.x; item < a.items; item += grid) {
+      DecodeCursor cur;
+      decode_cursor_init(a, cur);
+      DecodeSegment sg;
+      while (decode_next<D>(a, cur, sg)) {
         int b, rb, s, h;
-        decode_item(item, a.heads, a.splits, a.row_blocks, a.order, b, rb, s, h);
+        decode_item(sg.item, a.heads, a.splits, a.row_blocks, a.order, b, rb, s, h);
         const int len = a.lengths[b];
         const int last_row = min(rb * kRows + kRows, a.sq) - 1;
         const int end_tok = a.causal ? max(len - a.sq + last_row + 1, 0) : len;
         const int tiles = (end_tok + S::kTile - 1) / S::kTile;
-        const int t_begin = (int)((long long)tiles * s / a.splits);
-        const int t_end = (int)((long long)tiles * (s + 1) / a.splits);
+        int t_begin, t_end;
+        segment_range(sg, tiles, s, a.splits, t_begin, t_end);
         const int32_t* row_table = a.table + (long long)b * a.width;
         for (int t = t_begin; t < t_end; ++t, ++it) {
           const int stage = it % kStages;
@@ -164,9 +259,12 @@ __global__ void __launch_bounds__(DecodeShape<D>::kThreads, 1)
   bool ok = true;
   uint32_t it = 0;
 
-  for (long long item = blockIdx.x; item < a.items; item += grid) {
+  DecodeCursor cur;
+  decode_cursor_init(a, cur);
+  DecodeSegment sg;
+  while (decode_next<D>(a, cur, sg)) {
     int b, rb, s, h;
-    decode_item(item, a.heads, a.splits, a.row_blocks, a.order, b, rb, s, h);
+    decode_item(sg.item, a.heads, a.splits, a.row_blocks, a.order, b, rb, s, h);
     const int len = a.lengths[b];
     const int q0 = rb * kRows;
     int vis[kRows];
@@ -178,8 +276,8 @@ __global__ void __launch_bounds__(DecodeShape<D>::kThreads, 1)
       end_tok = max(end_tok, vis[r]);
     }
     const int tiles = (end_tok + S::kTile - 1) / S::kTile;
-    const int t_begin = (int)((long long)tiles * s / a.splits);
-    const int t_end = (int)((long long)tiles * (s + 1) / a.splits);
+    int t_begin, t_end;
+    segment_range(sg, tiles, s, a.splits, t_begin, t_end);
     const int nrows = min(kRows, a.sq - q0);  // query rows of this item that exist
 
     // Query rows for this lane's chunks, pre-scaled into the base-2 score domain.
@@ -355,6 +453,16 @@ __global__ void __launch_bounds__(DecodeShape<D>::kThreads, 1)
       }
     }
     named_barrier_sync(1, consumer_threads);
+    // A piece of an item cut between CTAs (contiguous schedule) writes its partial to its program's slot.
+    long long my_slot = 0;
+    int pieces = 1, q_first = 0, first_extra = 0;
+    if (sg.piece) {
+      const long long total = a.prog_u[a.programs];
+      q_first = program_of(total, a.programs, sg.item_u);
+      pieces = program_of(total, a.programs, sg.item_u + sg.units - 1) - q_first + 1;
+      first_extra = sg.item_u != program_start(total, a.programs, q_first) ? 1 : 0;
+      my_slot = piece_slot(q_first, first_extra, static_cast<int>(blockIdx.x) - q_first);
+    }
     for (int idx = threadIdx.x; idx < kRows * D; idx += consumer_threads) {
       const int r = idx / D;
       const int d = idx % D;
@@ -376,11 +484,57 @@ __global__ void __launch_bounds__(DecodeShape<D>::kThreads, 1)
       }
       const long long row_id = ((long long)b * a.sq + qi) * a.heads + h;
       const float val = den > 0.f ? num / den : 0.f;
-      if (a.write_partials) {
+      if (sg.piece) {
+        a.slot_o[(my_slot * kRows + r) * D + d] = val;
+        if (d == 0) a.slot_lse[my_slot * kRows + r] = den > 0.f ? mx + fast_log2(den) : kEmptyLse;
+      } else if (a.write_partials) {
         a.part_o[(row_id * a.splits + s) * D + d] = val;
         if (d == 0) a.part_lse[row_id * a.splits + s] = den > 0.f ? mx + fast_log2(den) : kEmptyLse;
       } else {
         reinterpret_cast<T*>(a.out)[row_id * D + d] = Tr::from_float(val);
+      }
+    }
+    if (sg.piece) {
+      // Piece merge in place: every piece publishes its partial, then counts itself in on the item's counter;
+      // the piece whose arrival completes the set merges all pieces from their slots in piece order (the split
+      // merge's arithmetic), so the output does not depend on which CTA finished last. No CTA waits for another.
+      __shared__ int piece_merge_here;
+      __threadfence();
+      named_barrier_sync(1, consumer_threads);
+      if (threadIdx.x == 0) piece_merge_here = atomicAdd(&a.counters[sg.item], 1) + 1 == pieces;
+      named_barrier_sync(1, consumer_threads);
+      if (piece_merge_here) {
+        __threadfence();
+        if (threadIdx.x == 0) a.counters[sg.item] = 0;  // ready for the next launch
+        for (int idx = threadIdx.x; idx < kRows * D; idx += consumer_threads) {
+          const int r = idx / D;
+          const int d = idx % D;
+          const int qi = q0 + r;
+          if (qi >= a.sq) continue;
+          float peak = kEmptyLse, total = 0.f, accm = 0.f;
+          constexpr int kChunk = 8;  // pieces whose loads are in flight together
+          for (int k0 = 0; k0 < pieces; k0 += kChunk) {
+            float lse[kChunk], o[kChunk];
+#pragma unroll
+            for (int c = 0; c < kChunk; ++c) {
+              if (k0 + c < pieces) {
+                const long long slot = piece_slot(q_first, first_extra, k0 + c);
+                lse[c] = __ldcg(a.slot_lse + slot * kRows + r);
+                o[c] = __ldcg(a.slot_o + (slot * kRows + r) * D + d);
+              }
+            }
+#pragma unroll
+            for (int c = 0; c < kChunk; ++c) {
+              if (k0 + c < pieces) {
+                float w_old, w_new;
+                merge_split_weights(lse[c], peak, total, w_old, w_new);
+                accm = merge_split_accumulate(accm, w_old, w_new, o[c]);
+              }
+            }
+          }
+          const long long row_id = ((long long)b * a.sq + qi) * a.heads + h;
+          reinterpret_cast<T*>(a.out)[row_id * D + d] = Tr::from_float(merge_split_finish(accm, total));
+        }
       }
     }
     if (a.fused_merge) {
@@ -445,14 +599,14 @@ static cudaError_t launch_decode_t(const LaunchDesc& d, const DecodeArgs& args, 
   if (err != cudaSuccess) return err;
   long long grid = args.items;
   const long long cap = d.p.grid_cap > 0 ? d.p.grid_cap : d.sm_count;
-  grid = std::min(grid, cap);
+  grid = args.contiguous ? args.programs : std::min(grid, cap);
   if (grid <= 0) return cudaSuccess;
   kernel<<<(unsigned)grid, S::kThreads, M::kBytes, d.stream>>>(kmap, vmap, args);
   return cudaGetLastError();
 }
 
 // Tokens per pipeline stage of the decode kernel for this head dimension (the TMA box rows must divide it).
-static int decode_tile_tokens(int head_dim) {
+int decode_tile_tokens(int head_dim) {
   switch (head_dim) {
 #define FGW_TILE_CASE(DD) \
   case DD:                \
@@ -552,6 +706,15 @@ cudaError_t launch_decode(const LaunchDesc& d, bool write_partials, bool fused_m
   args.write_partials = write_partials ? 1 : 0;
   args.fused_merge = (write_partials && fused_merge && d.merge_counters != nullptr) ? 1 : 0;
   args.merge_counters = d.merge_counters;
+  args.contiguous = d.contiguous ? 1 : 0;
+  args.programs = d.contiguous ? d.programs : 0;
+  args.tail_start = d.contiguous ? d.tail_start : 0;
+  args.prog_item = d.prog_item;
+  args.prog_off = d.prog_off;
+  args.prog_u = d.prog_u;
+  args.counters = d.counters;
+  args.slot_lse = d.slot_lse;
+  args.slot_o = d.slot_o;
   args.items = (long long)p.batch * args.row_blocks * p.num_splits * p.heads;
   args.scale_log2 = (1.0f / sqrtf((float)p.head_dim)) * kLog2e;
   args.budget_ns = d.budget_ns;

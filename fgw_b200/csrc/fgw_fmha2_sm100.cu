@@ -195,17 +195,6 @@ __device__ __forceinline__ bool next_segment(const Fmha2Args& a, SegmentCursor& 
   return true;
 }
 
-// Contiguous schedule: program p owns units [start(p), start(p + 1)), start(p) = p (T / G) + min(p, T % G).
-__device__ __forceinline__ long long program_start(long long total, int programs, int p) {
-  return static_cast<long long>(p) * (total / programs) + min(static_cast<long long>(p), total % programs);
-}
-
-__device__ __forceinline__ int program_of(long long total, int programs, long long u) {
-  const long long b = total / programs, r = total % programs;
-  if (u < r * (b + 1)) return static_cast<int>(u / (b + 1));
-  return static_cast<int>(r + (u - r * (b + 1)) / b);
-}
-
 template <typename T, int NB>
 __global__ void __launch_bounds__(384, 1)
     fmha2_sm100_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,

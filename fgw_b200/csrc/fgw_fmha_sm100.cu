@@ -572,8 +572,14 @@ cudaError_t launch_tensor(const LaunchDesc& d, bool write_partials) {
       !make_kv_sw_map(&vmap, p.v_cache, p, args.box_rows)) {
     return cudaErrorInvalidValue;
   }
-  if (nb <= 2 && d.key_halves) return launch_tensor_halves(d, write_partials, qmap, kmap, vmap, args.box_rows);
-  if (nb <= 2 && !d.single_tile) return launch_tensor_pairs(d, write_partials, qmap, kmap, vmap, args.box_rows);
+  if (d.tensor_kernel == FGW_TENSOR_KERNEL_HALVES) {
+    if (nb > 2) return cudaErrorNotSupported;
+    return launch_tensor_halves(d, write_partials, qmap, kmap, vmap, args.box_rows);
+  }
+  if (d.tensor_kernel == FGW_TENSOR_KERNEL_PAIRS) {
+    if (nb > 2) return cudaErrorNotSupported;
+    return launch_tensor_pairs(d, write_partials, qmap, kmap, vmap, args.box_rows);
+  }
   const bool bf16 = p.dtype == FGW_DTYPE_BFLOAT16;
   switch (nb) {
     case 1:

@@ -38,22 +38,31 @@ struct LaunchDesc {
   long long* prog_u;   // [programs + 1]
   long long* prefix;   // [items + 1] plan scratch: first unit of every item
   int32_t* counters;   // [items]
-  float* slot_lse;     // [2 * programs, kPairRows] base-2 LSE of each piece row
-  float* slot_o;       // [2 * programs, kPairRows, head_dim] FP32 normalised piece outputs
+  int slot_rows;       // query rows per slot (stream_slot_rows)
+  float* slot_lse;     // [2 * programs, slot_rows] base-2 LSE of each piece row
+  float* slot_o;       // [2 * programs, slot_rows, head_dim] FP32 normalised piece outputs
   // split-KV on the decode path: one arrival counter per (request, row block, head) group, so the CTA that
   // completes a group's split set merges it in the same launch (zeroed by plan_kernel)
   int32_t* merge_counters;  // [batch * q_len * heads] (an upper bound on the groups)
   int merge_groups;         // 0 when there is nothing to zero
   uint64_t budget_ns;
   int sm_count;
-  bool single_tile;   // force the one-query-tile tensor kernel (FGW_MHA_TENSOR_SINGLE_TILE set)
-  bool key_halves;    // opt-in key-halves tensor kernel for head_dim <= 128 (FGW_MHA_TENSOR_KERNEL=halves)
+  int tensor_kernel;  // fgw_tensor_kernel the tensor path runs (resolve_tensor_kernel)
   cudaStream_t stream;
 };
 
 // Work items of the two-tile tensor kernel: batch x heads x splits x ceil(q_len / 256).
 long long pair_items(const fgw_mha_params& p);
-// Whether the main launch runs the contiguous schedule (the two-tile kernel with fused piece merge).
+// Query rows of one decode work item, and tokens of one decode pipeline stage (fgw_decode.cu).
+int decode_rows_per_item(int head_dim);
+int decode_tile_tokens(int head_dim);
+// Work items the contiguous schedule lays end to end: the two-tile kernel's on the tensor path, the decode
+// kernel's (request, query-row block, head) on the decode path.
+long long stream_items(const fgw_mha_params& p);
+// Query rows of one partial slot of the contiguous schedule: one two-tile item, or one decode item.
+int stream_slot_rows(const fgw_mha_params& p);
+// Whether the main launch runs the contiguous schedule (fused piece merge): the two-tile tensor kernel, or
+// the decode kernel, with one split.
 bool use_stream_schedule(const fgw_mha_params& p);
 
 // Workspace layout: header | lens | order | part_lse | part_o | (contiguous schedule: prog_item | prog_off |
@@ -78,8 +87,9 @@ cudaError_t launch_tensor_pairs(const LaunchDesc& d, bool write_partials, const 
 cudaError_t launch_tensor_halves(const LaunchDesc& d, bool write_partials, const CUtensorMap& qmap,
                                  const CUtensorMap& kmap, const CUtensorMap& vmap, int box_rows);
 
-// Which path AUTO picks.
+// Which path AUTO picks, and which tcgen05 kernel the tensor path runs.
 int resolve_path(const fgw_mha_params& p);
+int resolve_tensor_kernel(const fgw_mha_params& p);
 
 // Tensor-map encoder from the driver (resolved once through the runtime).
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,

@@ -70,9 +70,23 @@ def decode_rows(dim):
     return 1 if per_lane >= 32 else (2 if per_lane >= 16 else 4)
 
 
-def _features_b200(batch, sq, heads, dim, lengths, splits, cores):
+def tile_stats(lengths):
+    """(sum, max) over the requests of their caches' 128-token KV tiles: all the version-3 model reads of the
+    lengths, so a serving loop whose lengths change every step computes these once per call."""
+    if len(lengths) > 64:
+        import numpy as np
+        tiles = (np.asarray(lengths, dtype=np.int64) + (KV_TILE - 1)) // KV_TILE
+        return int(tiles.sum()), int(tiles.max())
     tiles = [(n + KV_TILE - 1) // KV_TILE for n in lengths]
-    mean_tiles = sum(tiles) / batch
+    return sum(tiles), max(tiles)
+
+
+def _features_b200(batch, sq, heads, dim, lengths, splits, cores):
+    return _features_b200_stats(batch, sq, heads, dim, *tile_stats(lengths), splits, cores)
+
+
+def _features_b200_stats(batch, sq, heads, dim, tiles_sum, tiles_max, splits, cores):
+    mean_tiles = tiles_sum / batch
     decode = sq <= DECODE_MAX_QUERIES
     rows = decode_rows(dim) if decode else PAIR_ROWS
     items = batch * heads * ((sq + rows - 1) // rows) * splits
@@ -86,7 +100,7 @@ def _features_b200(batch, sq, heads, dim, lengths, splits, cores):
     else:
         waves = (items + cores - 1) // cores
         serial = waves * math.ceil(mean_tiles / splits)
-    longest = (max(tiles) + splits - 1) // splits
+    longest = (tiles_max + splits - 1) // splits
     multi = 1 if splits > 1 else 0
     return [1.0,
             float(serial) if decode else 0.0,
@@ -182,3 +196,21 @@ def pick_within_tolerance(costs, model):
     else:
         limit = best + max(best * tolerance, model.get("absolute_selection_margin_us", 0.0))
     return min(s for s, value in costs.items() if value <= limit)
+
+
+def select_b200_splits(batch, sq, heads, dim, page_size, width, tiles_sum, tiles_max, model=None, cores=None):
+    """``select_model_splits`` of the version-3 (B200) model from ``tile_stats`` of the lengths instead of the
+    lengths themselves (the same choice; the caller has checked the lengths against the table)."""
+    model = load_model(3) if model is None else model
+    if model["version"] != 3:
+        raise ValueError("select_b200_splits takes the version-3 model")
+    cores = model.get("cores", 28) if cores is None else cores
+    capacity_tiles = (page_size * width + KV_TILE - 1) // KV_TILE
+    floor = model["latency_floor_us"]
+    costs = {}
+    for s in B200_SPLITS:
+        if s <= capacity_tiles:
+            raw = sum(a * b for a, b in zip(_features_b200_stats(batch, sq, heads, dim, tiles_sum, tiles_max, s,
+                                                                 cores), model["weights"]))
+            costs[s] = max(raw, floor["multi" if s > 1 else "single"])
+    return pick_within_tolerance(costs, model)

@@ -20,8 +20,8 @@ callable; the CUDA kernels size their own TMA rings, so they do not change the s
 ``persistent_programs`` caps the persistent grid (default: the SM count; ``None`` uncapped).
 """
 import functools
-import os
 
+import numpy as np
 import torch
 
 from fgw_b200 import _native
@@ -33,6 +33,9 @@ DEFAULT_PROGRAMS = "sm_count"
 DECODE_MAX_QUERIES = 8  # query rows per request at or below which AUTO uses the decode kernel
 BLOCK_Q_TENSOR = 128
 BLOCK_KV = 128
+# tcgen05 kernels of the tensor path (fgw_tensor_kernel): auto = pairs up to D128, single above
+TENSOR_KERNELS = {"auto": _native.TENSOR_KERNEL_AUTO, "pairs": _native.TENSOR_KERNEL_PAIRS,
+                  "single": _native.TENSOR_KERNEL_SINGLE, "halves": _native.TENSOR_KERNEL_HALVES}
 
 
 def _decode_rows(dim):
@@ -83,8 +86,11 @@ def _b200_model():
     return general_model.load_model(3)  # the B200 feature set fitted on B200 split sweeps
 
 
-def _select_auto_splits(batch, sq, heads, dim, width, page_size, lengths, cores):
-    """B200 split choice from host-known lengths (or table capacity) with the fitted B200 model."""
+def _select_auto_splits(batch, sq, heads, dim, width, page_size, lengths, cores, chosen=None):
+    """B200 split choice from host-known lengths (or table capacity) with the fitted B200 model; ``chosen`` is
+    that choice when the caller has already made it."""
+    if chosen is not None:
+        return chosen
     if lengths is None:
         lengths = (width * page_size,) * batch
     return general_model.select_model_splits(batch, sq, heads, dim, page_size, width, list(lengths),
@@ -96,8 +102,13 @@ def build_kernel(batch, sq, heads, dim, pool_rows, width, page_size, causal, dty
                  pipeline_stages=2, buffer_versions=2, q_resident=True, kv_versions=None, dump_ir_dir=None,
                  schedule_mode="manual", num_splits=None, split_policy="auto", full_kv_cache=False,
                  persistent_programs=DEFAULT_PROGRAMS, cube_mode="stable", cache_lengths=None,
-                 general_model_version=1, task_assignment=None, path="auto", _b200_splits=None):
+                 general_model_version=1, task_assignment=None, path="auto", tensor_kernel="auto",
+                 _b200_splits=None, _auto_splits=None):
     """Validate a static shape, pick the split count and return a launch callable.
+
+    ``_auto_splits`` is the B200 model's choice already made by the caller from the lengths' tile statistics
+    (``mha_paged_decode`` does this, so launchers are cached per shape and split count, not per length list);
+    it stands in for the model wherever the policy would run it.
 
     ``_b200_splits`` (B200-only, for measuring the split model's candidates) fixes the split count to one of
     ``general_split_cost_model.B200_SPLITS``, including the 64 and 128 that ``split_policy="auto"`` may pick but
@@ -121,6 +132,8 @@ def build_kernel(batch, sq, heads, dim, pool_rows, width, page_size, causal, dty
         raise ValueError("split_policy must be auto, legacy or cost_model")
     if path not in ("auto", "decode", "tensor"):
         raise ValueError("path must be auto, decode or tensor")
+    if tensor_kernel not in TENSOR_KERNELS:
+        raise ValueError("tensor_kernel must be one of " + ", ".join(TENSOR_KERNELS))
     selected_route = route(dtype, dim, page_size, sq, causal, cube_mode)
     if selected_route == "cube_general":
         if (pipeline_stages != 2 or buffer_versions != 2 or not q_resident or kv_versions is not None
@@ -153,16 +166,15 @@ def build_kernel(batch, sq, heads, dim, pool_rows, width, page_size, causal, dty
         capacity_tiles = (capacity_tokens + 31) // 32
         tasks = batch * heads * ((sq + 31) // 32)
         if num_splits is None and split_policy == "cost_model":
-            if cache_lengths is None:
+            if cache_lengths is None and _auto_splits is None:
                 raise ValueError("Experimental cost model requires host-known cache_lengths")
-            splits = general_model.select_model_splits(batch, sq, heads, dim, page_size, width, list(cache_lengths),
-                                                       model=_b200_model(), cores=cores)
+            splits = _select_auto_splits(batch, sq, heads, dim, width, page_size, cache_lengths, cores, _auto_splits)
             policy_name = "cost_model"
         elif num_splits is None and split_policy == "auto":
             # The reference's rule here fills the cores (fill_28); over 148 SMs that over-splits (the config-3
             # sweep measured it 1.2-2.4x slower than the best split), so "auto" takes the fitted B200 model,
             # over table capacity when the lengths are not known on the host.
-            splits = _select_auto_splits(batch, sq, heads, dim, width, page_size, cache_lengths, cores)
+            splits = _select_auto_splits(batch, sq, heads, dim, width, page_size, cache_lengths, cores, _auto_splits)
             policy_name = "cost_model"
         else:
             splits = general_policy.select_splits(tasks, capacity_tiles, num_splits, target_programs=cores)
@@ -174,7 +186,7 @@ def build_kernel(batch, sq, heads, dim, pool_rows, width, page_size, causal, dty
             splits = v7_model.vector_fallback_splits(batch, sq, heads, width, page_size)
             policy_name = "legacy"
         else:
-            splits = _select_auto_splits(batch, sq, heads, dim, width, page_size, cache_lengths, cores)
+            splits = _select_auto_splits(batch, sq, heads, dim, width, page_size, cache_lengths, cores, _auto_splits)
             policy_name = "cost_model"
     else:
         if num_splits is not None and (type(num_splits) is not int or num_splits not in (1, 2, 4, 8, 16)):
@@ -188,7 +200,7 @@ def build_kernel(batch, sq, heads, dim, pool_rows, width, page_size, causal, dty
             splits = v7_model.legacy_splits(batch, sq, heads, width, page_size)
             policy_name = "legacy"
         else:
-            splits = _select_auto_splits(batch, sq, heads, dim, width, page_size, cache_lengths, cores)
+            splits = _select_auto_splits(batch, sq, heads, dim, width, page_size, cache_lengths, cores, _auto_splits)
             policy_name = "cost_model"
 
     kernel_path = {"auto": _native.PATH_AUTO, "decode": _native.PATH_DECODE, "tensor": _native.PATH_TENSOR}[path]
@@ -227,14 +239,12 @@ def build_kernel(batch, sq, heads, dim, pool_rows, width, page_size, causal, dty
     params.path = kernel_path
     params.schedule = {None: _native.SCHEDULE_AUTO, "strided": _native.SCHEDULE_STRIDED,
                        "contiguous": _native.SCHEDULE_CONTIGUOUS, "tail": _native.SCHEDULE_TAIL}[task_assignment]
+    params.tensor_kernel = TENSOR_KERNELS[tensor_kernel]
     workspace_bytes = _native.workspace_size(params)
-    # The contiguous schedule applies to the two-tile tensor kernel with one split (fgw_schedule in
-    # include/fgw_mha.h); elsewhere the work items are dealt out strided in longest-request-first order.
-    pair_items = batch * heads * ((sq + 255) // 256)
-    contiguous = (kernel_path == _native.PATH_TENSOR and dim <= 128 and splits == 1
-                  and task_assignment != "strided" and pair_items <= 65536
-                  and os.environ.get("FGW_MHA_TENSOR_SINGLE_TILE") != "1"
-                  and (task_assignment in ("contiguous", "tail") or 3 * pair_items < 2 * 148))
+    # The library resolves the schedule (fgw_schedule in include/fgw_mha.h): the contiguous cut where it applies,
+    # otherwise whole work items dealt out strided in longest-request-first order.
+    schedule = _native.resolve_schedule(params)
+    contiguous = schedule != _native.SCHEDULE_STRIDED
 
     def _bind(q, k, v, table, lengths, out):
         p = _native.Params.from_buffer_copy(params)
@@ -276,10 +286,11 @@ def build_kernel(batch, sq, heads, dim, pool_rows, width, page_size, causal, dty
 
     launch.block_q = block_q
     launch.compute_grid = compute_grid
-    launch.task_assignment = (task_assignment if task_assignment == "tail" else "contiguous") if contiguous \
-        else "strided"
+    launch.task_assignment = {_native.SCHEDULE_STRIDED: "strided", _native.SCHEDULE_CONTIGUOUS: "contiguous",
+                              _native.SCHEDULE_TAIL: "tail"}[schedule]
     if contiguous:
-        compute_grid = min(cores, 148) if grid_cap == 0 else min(grid_cap, cores, 148)
+        # one program per persistent CTA, at most the library's contiguous-schedule limit
+        compute_grid = min(cores if grid_cap == 0 else min(grid_cap, cores), general_model.STREAM_MAX_PROGRAMS)
         launch.compute_grid = compute_grid
     launch.compute_work = compute_work
     launch.persistent_programs = programs
@@ -290,6 +301,7 @@ def build_kernel(batch, sq, heads, dim, pool_rows, width, page_size, causal, dty
     launch.query_tile_tasks = tasks
     launch.execution_mode = "direct_single_split" if splits == 1 else "split_and_merge"
     launch.execution_path = "sm100_decode" if kernel_path == _native.PATH_DECODE else "sm100_tcgen05"
+    launch.tensor_kernel = tensor_kernel
     launch.reference_route = selected_route
     launch.workspace_bytes = workspace_bytes
     launch.schedule = {"schedule_mode": schedule_mode, "pipeline_stages": pipeline_stages,
@@ -334,29 +346,36 @@ def mha_paged_decode(q, k_cache, v_cache, block_table, cache_seqlens, page_size,
                      pipeline_stages=2, buffer_versions=2, q_resident=True, kv_versions=None,
                      schedule_mode="manual", num_splits=None, split_policy="auto",
                      persistent_programs=DEFAULT_PROGRAMS, cube_mode="stable", general_model_version=1,
-                     path="auto", cache_lengths=None, out=None, task_assignment=None):
+                     path="auto", cache_lengths=None, out=None, task_assignment=None, tensor_kernel="auto"):
     """Paged MHA forward: O[B,Sq,H,D] = softmax(Q K^T / sqrt(D)) V over each request's live pages.
 
-    ``cache_lengths`` may pass the host copy of ``cache_seqlens`` when the caller already has it;
-    otherwise it is read once from the device, as the reference does.
+    ``cache_lengths`` may pass the host copy of ``cache_seqlens`` (a sequence or a NumPy array) when the caller
+    already has it; otherwise it is read once from the device, as the reference does. Launchers are cached per
+    shape and split count, so a serving loop whose lengths change every call reuses them.
     """
     b, sq, h, d = _check_inputs(q, k_cache, v_cache, block_table, cache_seqlens)
     width = block_table.shape[1]
-    selected_route = route(q.dtype, d, page_size, sq, is_causal, cube_mode)
-    lengths = list(cache_lengths) if cache_lengths is not None else cache_seqlens.cpu().tolist()
-    if len(lengths) != b:
+    capacity = width * page_size
+    route(q.dtype, d, page_size, sq, is_causal, cube_mode)  # the reference's route checks (ValueError)
+    lengths = np.asarray(cache_lengths if cache_lengths is not None else cache_seqlens.cpu().numpy())
+    if lengths.shape != (b,):
         raise ValueError("metadata shape mismatch")
-    if any(n < 0 or n > width * page_size for n in lengths):
+    if b and (int(lengths.min()) < 0 or int(lengths.max()) > capacity):
         raise ValueError("Cache lengths must be within table capacity")
-    full_kv_cache = all(n == width * page_size for n in lengths)
-    model_lengths = tuple(int(n) for n in lengths)
-    kernel = build_kernel(b, sq, h, d, k_cache.shape[0], width, page_size, bool(is_causal),
-                          "float16" if q.dtype == torch.float16 else "bfloat16", q.device.index,
-                          pipeline_stages=pipeline_stages, buffer_versions=buffer_versions, q_resident=q_resident,
-                          kv_versions=kv_versions, schedule_mode=schedule_mode, num_splits=num_splits,
-                          split_policy=split_policy, full_kv_cache=full_kv_cache,
-                          persistent_programs=persistent_programs, cube_mode=cube_mode,
-                          cache_lengths=model_lengths if selected_route != "cube_bf16_d128" or not full_kv_cache
-                          else None,
-                          general_model_version=general_model_version, path=path, task_assignment=task_assignment)
+    full_kv_cache = bool(int(lengths.min()) == capacity)
+    dtype_name = "float16" if q.dtype == torch.float16 else "bfloat16"
+    # The B200 model reads the lengths only through their KV-tile sum and maximum: the choice is made here,
+    # so the launcher below is cached per shape and split count and a new length list costs no rebuild.
+    auto = None
+    if num_splits is None and split_policy != "legacy":
+        stats = general_model.tile_stats(lengths.tolist() if b <= 64 else lengths)
+        auto = general_model.select_b200_splits(b, sq, h, d, page_size, width, *stats, model=_b200_model(),
+                                                cores=sm_count(q.device.index))
+    kernel = build_kernel(b, sq, h, d, k_cache.shape[0], width, page_size, bool(is_causal), dtype_name,
+                          q.device.index, pipeline_stages=pipeline_stages, buffer_versions=buffer_versions,
+                          q_resident=q_resident, kv_versions=kv_versions, schedule_mode=schedule_mode,
+                          num_splits=num_splits, split_policy=split_policy, full_kv_cache=full_kv_cache,
+                          persistent_programs=persistent_programs, cube_mode=cube_mode, cache_lengths=None,
+                          general_model_version=general_model_version, path=path, task_assignment=task_assignment,
+                          tensor_kernel=tensor_kernel, _auto_splits=auto)
     return kernel(q, k_cache, v_cache, block_table, cache_seqlens, out=out)

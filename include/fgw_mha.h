@@ -37,7 +37,7 @@
 extern "C" {
 #endif
 
-#define FGW_MHA_ABI_VERSION 3
+#define FGW_MHA_ABI_VERSION 4
 
 #if defined(__GNUC__)
 #define FGW_API __attribute__((visibility("default")))
@@ -73,14 +73,14 @@ typedef enum fgw_path {
  *               in longest-request-first order.
  *   CONTIGUOUS: the KV tiles of all work items, laid end to end, are cut into one contiguous range per CTA
  *               of equal length (loads differ by at most one tile); an item cut between CTAs is computed in
- *               pieces whose partial results the CTA finishing last merges in the same launch. Tensor path
- *               with num_splits == 1 and head_dim <= 128 only.
+ *               pieces whose partial results the CTA finishing last merges in the same launch.
  *   TAIL:       STRIDED for the full waves (the first floor(items / G) * G items, G = the programs), then
  *               CONTIGUOUS over the items of the last, partial wave only (the reference's tail plan,
- *               static_schedule.py:83-116 `make_tail_plan`): only those items are cut into pieces. Same
- *               restrictions as CONTIGUOUS.
- *   AUTO:       CONTIGUOUS where it applies and there are fewer work items than 2/3 of 148 programs (whole
- *               items would leave SMs idle), STRIDED otherwise.
+ *               static_schedule.py:83-116 `make_tail_plan`): only those items are cut into pieces.
+ *   AUTO:       decode path with one split: CONTIGUOUS. Tensor path: CONTIGUOUS where it applies and there are
+ *               fewer work items than 2/3 of 148 programs (whole items would leave SMs idle), STRIDED otherwise.
+ * CONTIGUOUS and TAIL apply with num_splits == 1 to the decode kernel and to the PAIRS tensor kernel; elsewhere
+ * the launch runs STRIDED (fgw_mha_resolve_schedule reports which).
  */
 typedef enum fgw_schedule {
   FGW_SCHEDULE_AUTO = 0,
@@ -88,6 +88,20 @@ typedef enum fgw_schedule {
   FGW_SCHEDULE_CONTIGUOUS = 2,
   FGW_SCHEDULE_TAIL = 3
 } fgw_schedule;
+
+/* Which tcgen05 kernel runs the tensor path (no reference counterpart: FGW chooses its Cube kernel by route).
+ *   AUTO:   PAIRS for head_dim <= 128, SINGLE above.
+ *   PAIRS:  two 128-row query tiles per work item sharing every K/V tile (head_dim <= 128).
+ *   SINGLE: one 128-row query tile per work item, P through shared memory (any head_dim).
+ *   HALVES: one query tile per work item, S double-buffered in TMEM, the softmax split by key halves over two
+ *           warpgroups (head_dim <= 128, strided schedule only).
+ * A kernel that cannot serve the head_dim returns FGW_ERR_UNSUPPORTED. */
+typedef enum fgw_tensor_kernel {
+  FGW_TENSOR_KERNEL_AUTO = 0,
+  FGW_TENSOR_KERNEL_PAIRS = 1,
+  FGW_TENSOR_KERNEL_SINGLE = 2,
+  FGW_TENSOR_KERNEL_HALVES = 3
+} fgw_tensor_kernel;
 
 /*
  * Tensor contract (same as the reference, operators/mha/README.md:5):
@@ -122,7 +136,8 @@ typedef struct fgw_mha_params {
   int32_t path;        /* fgw_path */
   int32_t wait_budget_ms; /* device-side wait limit; 0 = default (2000 ms) */
   int32_t schedule;       /* fgw_schedule */
-  int32_t reserved[3];    /* must be zero */
+  int32_t tensor_kernel;  /* fgw_tensor_kernel */
+  int32_t reserved[2];    /* must be zero */
 } fgw_mha_params;
 
 /* ABI version of the loaded library (FGW_MHA_ABI_VERSION it was built with). */
@@ -136,6 +151,10 @@ FGW_API int fgw_mha_device_sm_count(int device, int* sm_count);
 
 /* Kernel path AUTO resolves to for these parameters (FGW_PATH_DECODE or FGW_PATH_TENSOR). */
 FGW_API int fgw_mha_resolve_path(const fgw_mha_params* params, int* path);
+
+/* Schedule the main launch takes for these parameters (FGW_SCHEDULE_STRIDED, _CONTIGUOUS or _TAIL): AUTO and
+ * requests a kernel cannot serve resolved as fgw_mha_paged_fwd resolves them. */
+FGW_API int fgw_mha_resolve_schedule(const fgw_mha_params* params, int* schedule);
 
 /* Bytes of device workspace fgw_mha_paged_fwd / fgw_mha_partial need for these parameters. */
 FGW_API int fgw_mha_workspace_size(const fgw_mha_params* params, size_t* bytes);

@@ -69,6 +69,38 @@ def test_contiguous_schedule_pieces_merge_to_the_oracle(schedule, causal, progra
     assert torch.equal(out, out2)
 
 
+@pytest.mark.parametrize("schedule,causal,programs,dim,sq", [
+    ("contiguous", False, 1, 128, 1), ("contiguous", False, 3, 128, 1), ("contiguous", False, 7, 64, 3),
+    ("contiguous", True, 5, 128, 8), ("contiguous", False, None, 256, 2), ("contiguous", True, None, 128, 4),
+    ("tail", False, 5, 128, 1), ("tail", True, 7, 64, 8), ("tail", False, None, 128, 1),
+    ("strided", False, None, 128, 1), ("strided", True, 3, 256, 5)])
+def test_decode_contiguous_schedule_pieces_merge_to_the_oracle(schedule, causal, programs, dim, sq):
+    # Decode kernel, one split: the KV stages of all (request, query-row block, head) items are cut into equal
+    # ranges per program, so long requests are cut into pieces held by several CTAs and merged in place by the
+    # one completing the set; empty and short requests cost one unit. Few programs force many cuts.
+    case = ("decode_pieces", 4, sq, 3, dim, 64, 64)  # B4 H3, page 64, up to 4096 tokens
+    from fixtures import make_inputs, poison_unread
+    q, k, v, table = make_inputs(case, 7, torch.bfloat16)
+    lengths = [4000, 0, 1, 777]
+    k, v = poison_unread(k, v, table, lengths, 64)
+    inputs = {"case": case, "seed": 7, "dtype": torch.bfloat16, "causal": causal, "pattern": "decode_pieces",
+              "q": q, "k": k, "v": v, "table": table, "lengths": torch.tensor(lengths, dtype=torch.int32)}
+    from fgw_b200.operators.mha.current import build_kernel
+    dev = torch.device("cuda", 0)
+    args = [inputs[key].to(dev) for key in ("q", "k", "v", "table", "lengths")]
+    kwargs = dict(path="decode", task_assignment=schedule, _b200_splits=1)  # one split (page 64: fallback route)
+    if programs is not None:
+        kwargs["persistent_programs"] = programs
+    kernel = build_kernel(4, sq, 3, dim, k.shape[0], 64, 64, causal, "bfloat16", 0, **kwargs)
+    assert kernel.num_splits == 1 and kernel.task_assignment == schedule
+    out = kernel(*args)
+    torch.cuda.synchronize()
+    _check(out, oracle_output(inputs), inputs)
+    out2 = kernel(*args)  # the arrival counters are reset for the next launch
+    torch.cuda.synchronize()
+    assert torch.equal(out, out2)
+
+
 SPLIT_ENTRIES = [e for e in ENTRIES if e["seed"] == 7 and e["pattern"] == "mixed"]
 
 

@@ -26,7 +26,7 @@ def test_library_loads_and_exports_every_declared_symbol():
     lib = _native.library()
     for name in declared_functions():
         assert hasattr(lib, name), name
-    assert _native.abi_version() == _native.ABI_VERSION == 3
+    assert _native.abi_version() == _native.ABI_VERSION == 4
 
 
 def test_status_strings():
@@ -36,9 +36,10 @@ def test_status_strings():
 
 
 def test_params_struct_layout_matches_header():
-    # int64 pool_rows after six pointers; 13 int32 fields (the last is schedule) + 3 reserved.
+    # int64 pool_rows after six pointers; 14 int32 fields (schedule, then tensor_kernel) + 2 reserved.
     assert _native.Params.pool_rows.offset == 6 * 8
     assert _native.Params.schedule.offset == 6 * 8 + 8 + 12 * 4
+    assert _native.Params.tensor_kernel.offset == 6 * 8 + 8 + 13 * 4
     assert ctypes.sizeof(_native.Params) == 6 * 8 + 8 + 16 * 4
 
 
@@ -75,7 +76,7 @@ def _params(**overrides):
 
 
 def test_workspace_size_grows_with_splits():
-    one = _native.workspace_size(_params(num_splits=1))
+    one = _native.workspace_size(_params(num_splits=1, schedule=_native.SCHEDULE_STRIDED))
     four = _native.workspace_size(_params(num_splits=4))
     rows = 2 * 1 * 2
     assert four - one >= rows * 4 * (128 + 1) * 4
@@ -92,9 +93,9 @@ def test_split_decode_workspace_holds_one_arrival_counter_per_row():
     tensor = _native.workspace_size(_params(path=_native.PATH_TENSOR, **shape))
     assert decode - tensor == -(-rows * 4 // 256) * 256
     single = dict(shape, num_splits=1)
-    assert (_native.workspace_size(_params(path=_native.PATH_DECODE, **single))
-            == _native.workspace_size(_params(path=_native.PATH_TENSOR, schedule=_native.SCHEDULE_STRIDED,
-                                              **single)))
+    strided = dict(single, schedule=_native.SCHEDULE_STRIDED)
+    assert (_native.workspace_size(_params(path=_native.PATH_DECODE, **strided))
+            == _native.workspace_size(_params(path=_native.PATH_TENSOR, **strided)))
 
 
 @pytest.mark.parametrize("override", [dict(head_dim=24), dict(head_dim=272), dict(page_size=24),
@@ -155,3 +156,24 @@ def test_gather_argument_checks_without_a_device():
     g = _gather()
     g.reserved[1] = 1
     assert _gather_status(g) == _native.ERR_INVALID_ARGUMENT
+
+
+def test_resolved_schedule_per_path_and_kernel():
+    # decode path with one split: the contiguous cut (slots of the decode kernel's query rows); with splits, or
+    # when STRIDED is asked for, whole items
+    decode = dict(batch=256, heads=32, q_len=1, num_splits=1, path=_native.PATH_DECODE)
+    assert _native.resolve_schedule(_params(**decode)) == _native.SCHEDULE_CONTIGUOUS
+    assert _native.resolve_schedule(_params(**dict(decode, num_splits=2))) == _native.SCHEDULE_STRIDED
+    assert _native.resolve_schedule(_params(schedule=_native.SCHEDULE_STRIDED, **decode)) == _native.SCHEDULE_STRIDED
+    assert _native.resolve_schedule(_params(schedule=_native.SCHEDULE_TAIL, **decode)) == _native.SCHEDULE_TAIL
+    slots = 2 * 148 * 1 * (128 + 1) * 4  # D128 decode items carry one query row
+    assert (_native.workspace_size(_params(**decode))
+            >= _native.workspace_size(_params(schedule=_native.SCHEDULE_STRIDED, **decode)) + slots)
+    # tensor path: the two-tile kernel takes the contiguous cut; the single-tile and key-halves kernels do not
+    tensor = dict(q_len=4096, num_splits=1, path=_native.PATH_TENSOR, schedule=_native.SCHEDULE_CONTIGUOUS)
+    assert _native.resolve_schedule(_params(**tensor)) == _native.SCHEDULE_CONTIGUOUS
+    for kernel in (_native.TENSOR_KERNEL_SINGLE, _native.TENSOR_KERNEL_HALVES):
+        assert _native.resolve_schedule(_params(tensor_kernel=kernel, **tensor)) == _native.SCHEDULE_STRIDED
+    with pytest.raises(_native.FgwError):
+        _native.check(_native.library().fgw_mha_paged_fwd(ctypes.byref(_params(tensor_kernel=4)), None, 0, None),
+                      "fgw_mha_paged_fwd")
