@@ -1,20 +1,32 @@
-// Tensor-core paged attention with the softmax split by key halves (head dims up to 128). Opt-in:
-// launched only when FGW_MHA_TENSOR_KERNEL=halves is set in the environment; the two-query-tile kernel
-// (fgw_fmha2_sm100.cu) stays the default, since it is still the faster one on the long-query workload.
+// Tensor-core paged attention with the softmax split by key halves (head dims up to 128): the tensor path's
+// FGW_TENSOR_KERNEL_HALVES.
 //
-// Same contract, masking rules and epilogues as the other tensor kernels; the reference body it stands for
-// is operators/mha/kernels/mha_paged_decode_ascend_v7.py:225-315, 375-465. What changes is how the softmax
-// meets the tensor core:
-//   * one 128-row query tile per work item (request, head, split, query tile); S is double-buffered in
-//     TMEM, so QK of tile j + 2 is issued as soon as both halves of P(j) are consumed and the softmax of
-//     tile j + 1 never waits for the tensor core;
-//   * two softmax warpgroups: warps 4-7 own keys [0, 64) of every 128-key tile, warps 8-11 keys [64, 128).
-//     Each keeps its own running max and sum and its own O accumulator (O_0, O_1 in TMEM), like two
-//     interleaved KV splits, so the warpgroups never exchange a row max inside the loop; the epilogue
-//     merges the two halves with their LSE weights;
-//   * P of each half goes back into the first 32 TMEM columns of that half of S, and PV_h reads it from
-//     there (tcgen05.mma with the A operand in tensor memory).
+// Same contract, masking rules and epilogues as the other tensor kernels; the reference body it stands for is
+// operators/mha/kernels/mha_paged_decode_ascend_v7.py:225-315, 375-465. The schedule:
+//   * one 128-row query tile per work item (request, head, split, query tile); the CTA's items form one global
+//     sequence of KV tiles g = 0, 1, ...; S is double-buffered in TMEM (S[g % 2]), so QK(g + 2) is issued right
+//     after PV(g) and the softmax of tile g + 1 never waits for the tensor core;
+//   * two softmax warpgroups: warps 4-7 own keys [0, 64) of every 128-key tile, warps 8-11 keys [64, 128). Each
+//     keeps its own running max and sum and its own O accumulator (O_0, O_1 in TMEM), like two interleaved KV
+//     splits, so the warpgroups never exchange a row max inside the loop; the epilogue merges the two halves
+//     with their LSE weights;
+//   * P of each half goes back into the first 32 TMEM columns of that half of S, and PV_h reads it from there
+//     (tcgen05.mma with the A operand in tensor memory);
+//   * one shared-memory stage per tile holds V(g) and K(g + 2) (stage u = g + 2 holds V(u - 2) and K(u); the first
+//     two stages of the sequence hold K only), so the MMA warp waits on one barrier per tile, and a stage is free
+//     once QK(u) has completed (the commit that publishes S also releases the stage: QK(u) is issued after
+//     PV(u - 2));
+//   * the softmax warps hand P(g) to the MMA warp through a named barrier (bar.arrive / bar.sync) instead of an
+//     mbarrier the issuing thread polls; the MMA warp runs as a whole warp, one lane issuing;
+//   * Q is double-buffered, so the next item's first two QKs run while this item's epilogue reads O.
 // TMEM: S0 [0, 128), S1 [128, 256), O_0 [256, 256 + D), O_1 [384, 384 + D) of 512 columns.
+//
+// Barrier phases. Every parity wait below is on a phase that cannot be two completions old: s_full[b] completes
+// once per QK into S[b], and QK(g + 2) needs P(g), which its waiters have not released yet; pv_done completes
+// once per tile and a softmax warp that rescales at tile g + 1 has seen S(g + 1), whose QK was issued after
+// PV(g - 1), so at most PV(g) is outstanding; o_full completes once per non-empty item and the next item's last
+// PV needs this item's epilogue first; full[s] completes once per stage and stage u + 2 reuses the slot only
+// after QK(u). The producer waits on s_full for a stage's release, which needs exactly two stages in the ring.
 #include <algorithm>
 
 #include "fgw_common.cuh"
@@ -38,29 +50,32 @@ struct HalvesArgs {
 
 template <int NB>
 struct HalvesShape {
-  static constexpr int kBN = 128;                 // keys per KV tile; each softmax warpgroup owns 64
-  static constexpr int kTileBytes = 128 * 128;    // one 64-column block of a 128-row operand
-  static constexpr int kQBytes = NB * kTileBytes;
-  static constexpr int kKVBytes = NB * kBN * 128;  // one K (or V) stage
-  static constexpr int kStages = NB == 1 ? 4 : 2;
+  static constexpr int kBN = 128;                  // keys per KV tile; each softmax warpgroup owns 64
+  static constexpr int kTileBytes = 128 * 128;     // one 64-column block of a 128-row operand
+  static constexpr int kQBytes = NB * kTileBytes;  // one query tile
+  static constexpr int kKBytes = NB * kBN * 128;   // one K (or V) tile
+  static constexpr int kStageBytes = 2 * kKBytes;  // V(u - 2) at 0, K(u) at kKBytes
+  static constexpr int kStages = 2;                // the s_full release needs exactly two (see above)
   static constexpr int kThreads = 384;
   // registers per thread after the warpgroup split (4 x 32 x 88 + 8 x 32 x 208 = 384 x 168)
   static constexpr int kRegsControl = 88;
   static constexpr int kRegsSoftmax = 208;
-  // first TMEM column of O_h
   __device__ __forceinline__ static uint32_t o_col(int h) { return 256u + 128u * static_cast<uint32_t>(h); }
   static constexpr int kTmemCols = 512;
   // shared memory carve-up; kX: per half, the row max and row sum of every row, for the epilogue merge
   static constexpr int kQ = 0;
-  static constexpr int kK = kQ + kQBytes;
-  static constexpr int kV = kK + kStages * kKVBytes;
-  static constexpr int kX = kV + kStages * kKVBytes;
+  static constexpr int kStage = kQ + 2 * kQBytes;
+  static constexpr int kX = kStage + kStages * kStageBytes;
   static constexpr int kBar = kX + 2 * 2 * 128 * 4;
-  // q_full, q_empty, k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2], p_full[2], pv_done[2],
-  // o_empty, mma_done
-  static constexpr int kNumBars = 2 + 4 * kStages + 8;
+  // q_full[2], q_empty[2], full[kStages], s_full[2], pv_done, o_full, mma_done
+  static constexpr int kNumBars = 4 + kStages + 5;
   static constexpr int kTmemSlot = kBar + kNumBars * 8;
   static constexpr int kBytes = kTmemSlot + 16 + 1024;
+  // named barriers: P(g) handed over on kBarP + g % 2 (8 softmax warps arrive, the MMA warp syncs); the two
+  // warpgroups exchange their epilogue states on kBarX
+  static constexpr uint32_t kBarP = 4;
+  static constexpr uint32_t kBarPThreads = 9 * 32;
+  static constexpr uint32_t kBarX = 6;
 };
 
 struct HalvesItem {
@@ -86,6 +101,42 @@ __device__ __forceinline__ void halves_item(const HalvesArgs& a, long long item,
   c.n = static_cast<int>((long long)tiles * (c.s + 1) / a.splits) - c.n_begin;
 }
 
+// Walks the CTA's non-empty items tile by tile, `ahead` tiles ahead of a consumer: the producer and the MMA warp
+// need the item of tile g + 2 while they work on tile g.
+struct TileCursor {
+  long long next_item;  // next item to look at
+  HalvesItem c;         // current item
+  int j;                // tile within it
+  int items_seen;       // non-empty items entered so far (their Q buffer is (items_seen - 1) % 2)
+  bool valid;
+};
+
+__device__ __forceinline__ void tile_cursor_advance(const HalvesArgs& a, TileCursor& t) {
+  if (t.valid && t.j + 1 < t.c.n) {
+    ++t.j;
+    return;
+  }
+  t.valid = false;
+  while (t.next_item < a.items) {
+    halves_item(a, t.next_item, t.c);
+    t.next_item += gridDim.x;
+    if (t.c.n > 0) {
+      t.j = 0;
+      ++t.items_seen;
+      t.valid = true;
+      return;
+    }
+  }
+}
+
+__device__ __forceinline__ void tile_cursor_init(const HalvesArgs& a, TileCursor& t) {
+  t.next_item = blockIdx.x;
+  t.j = 0;
+  t.items_seen = 0;
+  t.valid = false;
+  tile_cursor_advance(a, t);
+}
+
 // 2^(s * scale - m) for the 64 scores of one half row (32 FP32 pairs, scale-and-subtract two lanes per
 // instruction), summed into four partial sums and packed to 16-bit pairs.
 template <typename Tr>
@@ -101,6 +152,10 @@ __device__ __forceinline__ void halves_exp2_pack(const uint32_t (&sr)[64], float
   }
 }
 
+__device__ __forceinline__ void named_barrier_arrive(uint32_t id, uint32_t threads) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
 template <typename T, int NB>
 __global__ void __launch_bounds__(384, 1)
     fmha_halves_sm100_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
@@ -108,45 +163,33 @@ __global__ void __launch_bounds__(384, 1)
   using S = HalvesShape<NB>;
   using Tr = ElemTraits<T>;
   constexpr int BN = S::kBN;
-  constexpr int NS = S::kStages;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* q_smem = smem + S::kQ;
-  uint8_t* k_smem = smem + S::kK;
-  uint8_t* v_smem = smem + S::kV;
+  uint8_t* st_smem = smem + S::kStage;
   float* xch = reinterpret_cast<float*>(smem + S::kX);  // [half][0: max, 1: sum][row]
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::kBar);
-  uint64_t* q_full = bars + 0;
-  uint64_t* q_empty = bars + 1;
-  uint64_t* k_full = bars + 2;
-  uint64_t* k_empty = k_full + NS;
-  uint64_t* v_full = k_empty + NS;
-  uint64_t* v_empty = v_full + NS;
-  uint64_t* s_full = v_empty + NS;   // [2]: S buffer b holds a tile's scores
-  uint64_t* p_full = s_full + 2;     // [2]: half h of P is in TMEM
-  uint64_t* pv_done = p_full + 2;    // [2]: PV_h of a tile has completed
-  uint64_t* o_empty = pv_done + 2;   // the epilogue has read O_0 and O_1
-  uint64_t* mma_done = o_empty + 1;
+  uint64_t* q_full = bars + 0;        // [2]
+  uint64_t* q_empty = bars + 2;       // [2]
+  uint64_t* full = bars + 4;          // [kStages]: a stage's V and K have landed
+  uint64_t* s_full = full + S::kStages;  // [2]: S[b] holds a tile's scores (and frees the stage of that QK)
+  uint64_t* pv_done = s_full + 2;     // PV of a tile has completed
+  uint64_t* o_full = pv_done + 1;     // the last PV of an item has completed
+  uint64_t* mma_done = o_full + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::kTmemSlot);
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
-    mbar_init(q_empty, 1);
-    for (int i = 0; i < NS; ++i) {
-      mbar_init(&k_full[i], 1);
-      mbar_init(&k_empty[i], 1);
-      mbar_init(&v_full[i], 1);
-      mbar_init(&v_empty[i], 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+      mbar_init(&s_full[i], 1);
     }
-    for (int t = 0; t < 2; ++t) {
-      mbar_init(&s_full[t], 1);
-      mbar_init(&p_full[t], 4);  // one arrival per warp of the half's warpgroup
-      mbar_init(&pv_done[t], 1);
-    }
-    mbar_init(o_empty, 8);  // every softmax warp
+    for (int i = 0; i < S::kStages; ++i) mbar_init(&full[i], 1);
+    mbar_init(pv_done, 1);
+    mbar_init(o_full, 1);
     mbar_init(mma_done, 1);
     fence_barrier_init();
   }
@@ -159,164 +202,184 @@ __global__ void __launch_bounds__(384, 1)
   tc_fence_after_sync();
   const uint32_t tmem = *tmem_slot;
   const int D = a.dim;
-  const long long grid = gridDim.x;
 
   if (warp < 4) setmaxnreg_dec<S::kRegsControl>();  // warpgroup 0: TMA, MMA and two idle warps
   if (warp == 0) {
     // ------------------------------------------------------------------------- TMA producer
+    // Stage u (ring slot u % 2) holds V(u - 2) and K(u) of the CTA's tile sequence; Q of each item goes into Q
+    // buffer (item % 2) just before the item's first K.
     if (lane == 0) {
       tma_prefetch_desc(&qmap);
       tma_prefetch_desc(&kmap);
       tma_prefetch_desc(&vmap);
       bool ok = true;
-      uint32_t kc = 0, vc = 0, qc = 0;
       const int boxes = BN / a.box_rows;
       const uint32_t box_bytes = a.box_rows * 128;
-      for (long long item = blockIdx.x; item < a.items; item += grid) {
-        HalvesItem c;
-        halves_item(a, item, c);
-        if (c.n <= 0) continue;
-        if (ok && !mbar_wait(q_empty, (qc & 1) ^ 1, a.budget_ns)) {
-          ok = false;
-          record_error(a.ws, FGW_ERR_DEVICE_TIMEOUT, 70);
-        }
-        if (ok) {
-          mbar_arrive_expect_tx(q_full, S::kQBytes);
-          for (int blk = 0; blk < NB; ++blk) {
-            tma_load_4d(q_smem + blk * S::kTileBytes, &qmap, q_full, blk * 64, c.h, c.q0, c.b);
-          }
-        }
-        ++qc;
+      auto fail = [&](int site) {
+        ok = false;
+        record_error(a.ws, FGW_ERR_DEVICE_TIMEOUT, site);
+      };
+      // the live boxes of tile j of item c, and their loads into dst
+      auto live_boxes = [&](const HalvesItem& c, int j) {
+        const int tok0 = (c.n_begin + j) * BN;
+        int nbox = 0;
+        for (int k = 0; k < boxes; ++k) nbox += (tok0 + k * a.box_rows < c.len) ? 1 : 0;
+        return nbox;
+      };
+      auto load_tile = [&](const CUtensorMap* map, const HalvesItem& c, int j, uint8_t* dst, uint64_t* bar,
+                           int nbox) {
         const int32_t* row_table = a.table + (long long)c.b * a.width;
-        for (int j = 0; j < c.n; ++j) {
-          const int tok0 = (c.n_begin + j) * BN;
-          int nbox = 0;
-          for (int k = 0; k < boxes; ++k) nbox += (tok0 + k * a.box_rows < c.len) ? 1 : 0;
-#pragma unroll
-          for (int which = 0; which < 2; ++which) {  // K tile, then V tile of KV step j
-            const uint32_t cnt = which == 0 ? kc : vc;
-            uint64_t* full = which == 0 ? k_full : v_full;
-            uint64_t* empty = which == 0 ? k_empty : v_empty;
-            const CUtensorMap* map = which == 0 ? &kmap : &vmap;
-            uint8_t* ring = which == 0 ? k_smem : v_smem;
-            const int st = cnt % NS;
-            if (ok && !mbar_wait(&empty[st], ((cnt / NS) & 1) ^ 1, a.budget_ns)) {
-              ok = false;
-              record_error(a.ws, FGW_ERR_DEVICE_TIMEOUT, 71 + which);
-            }
-            if (ok) {
-              mbar_arrive_expect_tx(&full[st], NB * nbox * box_bytes);
-              uint8_t* dst = ring + st * S::kKVBytes;
-              for (int k = 0; k < nbox; ++k) {
-                const int tok = tok0 + k * a.box_rows;
-                const int row = row_table[tok / a.page] * a.page + tok % a.page;
-                for (int blk = 0; blk < NB; ++blk) {
-                  tma_load_3d(dst + blk * BN * 128 + k * box_bytes, map, &full[st], blk * 64, c.h, row);
-                }
-              }
+        const int tok0 = (c.n_begin + j) * BN;
+        for (int k = 0; k < nbox; ++k) {
+          const int tok = tok0 + k * a.box_rows;
+          const int row = row_table[tok / a.page] * a.page + tok % a.page;
+          for (int blk = 0; blk < NB; ++blk) {
+            tma_load_3d(dst + blk * BN * 128 + k * box_bytes, map, bar, blk * 64, c.h, row);
+          }
+        }
+      };
+      TileCursor kc, vc;  // K(u) and V(u - 2)
+      tile_cursor_init(a, kc);
+      tile_cursor_init(a, vc);
+      uint32_t u = 0;
+      while (kc.valid || vc.valid) {
+        const int slot = u & 1;
+        // the slot's previous stage (u - 2) is free once QK(u - 2) has completed
+        if (ok && u >= 2 && !mbar_wait(&s_full[slot], ((u - 2) >> 1) & 1, a.budget_ns)) fail(70);
+        const bool has_k = kc.valid;
+        const bool has_v = u >= 2 && vc.valid;
+        if (has_k && kc.j == 0) {
+          // the item's Q, into buffer (items - 1) % 2, once the item two back has issued its last QK
+          const int qb = (kc.items_seen - 1) & 1;
+          if (ok && kc.items_seen > 2 && !mbar_wait(&q_empty[qb], ((kc.items_seen - 3) >> 1) & 1, a.budget_ns)) {
+            fail(71);
+          }
+          if (ok) {
+            mbar_arrive_expect_tx(&q_full[qb], S::kQBytes);
+            for (int blk = 0; blk < NB; ++blk) {
+              tma_load_4d(q_smem + qb * S::kQBytes + blk * S::kTileBytes, &qmap, &q_full[qb], blk * 64, kc.c.h,
+                          kc.c.q0, kc.c.b);
             }
           }
-          ++kc;
-          ++vc;
         }
+        const int kbox = has_k ? live_boxes(kc.c, kc.j) : 0;
+        const int vbox = has_v ? live_boxes(vc.c, vc.j) : 0;
+        if (ok) {
+          uint8_t* dst = st_smem + slot * S::kStageBytes;
+          mbar_arrive_expect_tx(&full[slot], NB * (kbox + vbox) * box_bytes);
+          if (has_v) load_tile(&vmap, vc.c, vc.j, dst, &full[slot], vbox);
+          if (has_k) load_tile(&kmap, kc.c, kc.j, dst + S::kKBytes, &full[slot], kbox);
+        }
+        if (has_k) tile_cursor_advance(a, kc);
+        if (has_v) tile_cursor_advance(a, vc);
+        ++u;
       }
+      // leave no copy in flight: the last two stages landed (or their waits gave up)
+      for (uint32_t w = (u >= 2 ? u - 2 : 0); w < u; ++w) mbar_wait(&full[w & 1], (w >> 1) & 1, a.budget_ns);
     }
   } else if (warp == 1) {
-    // ------------------------------------------------------------------------- UMMA issuer
-    if (lane == 0) {
-      bool ok = true;
-      uint32_t kc = 0, vc = 0, qc = 0, oc = 0, pc = 0, g = 0;  // g: tiles so far (S buffer g % 2)
-      const int fmt = Tr::kUmmaFormat;
-      const uint32_t idesc_qk = umma_idesc_f16(fmt, 128, BN, 0, 0);
-      const uint32_t idesc_pv = umma_idesc_f16(fmt, 128, D, 0, 1);
-      const uint32_t q_lo = umma_desc_lo(smem_u32(q_smem), 16);
-      const uint32_t k_lo = umma_desc_lo(smem_u32(k_smem), 16);
-      const uint32_t v_lo = umma_desc_lo(smem_u32(v_smem), BN * 128);
-      constexpr uint32_t kHi = umma_desc_hi(1024, 2);
-      const int ksteps_qk = D / 16;
-      auto wait_all_or_fail = [&](uint64_t* b0, uint32_t p0, uint64_t* b1, uint32_t p1, uint64_t* b2, uint32_t p2,
-                                  int site) {
-        if (ok && !mbar_wait_all(b0, p0, b1, p1, b2, p2, nullptr, 0, a.budget_ns)) {
-          ok = false;
-          record_error(a.ws, FGW_ERR_DEVICE_TIMEOUT, site);
-        }
-        return ok;
-      };
-      // S[buf] = Q K^T, K from stage `st` (already waited for); publishes S[buf] and frees the K stage.
-      auto qk = [&](uint32_t buf, int st) {
-        const uint32_t b_lo = k_lo + static_cast<uint32_t>((st * S::kKVBytes) >> 4);
+    // ------------------------------------------------------------------------- UMMA issuer (whole warp, lane 0
+    // issues; the warp takes part in the P named barriers)
+    bool ok = true;
+    const int fmt = Tr::kUmmaFormat;
+    const uint32_t idesc_qk = umma_idesc_f16(fmt, 128, BN, 0, 0);
+    const uint32_t idesc_pv = umma_idesc_f16(fmt, 128, D, 0, 1);
+    const uint32_t q_lo = umma_desc_lo(smem_u32(q_smem), 16);
+    const uint32_t k_lo = umma_desc_lo(smem_u32(st_smem + S::kKBytes), 16);
+    const uint32_t v_lo = umma_desc_lo(smem_u32(st_smem), BN * 128);
+    constexpr uint32_t kHi = umma_desc_hi(1024, 2);
+    const int ksteps_qk = D / 16;
+    auto wait_lane0 = [&](uint64_t* bar, uint32_t parity, int site) {
+      bool good = true;
+      if (lane == 0 && ok) {
+        good = mbar_wait(bar, parity, a.budget_ns);
+        if (!good) record_error(a.ws, FGW_ERR_DEVICE_TIMEOUT, site);
+      }
+      ok = __shfl_sync(0xffffffffu, ok && good, 0);
+      return ok;
+    };
+    // S[buf] = Q K^T with Q from buffer qb and K from the stage of slot `slot`; publishes S[buf] (and frees the
+    // stage for the producer).
+    auto qk = [&](uint32_t buf, int qb, int slot) {
+      if (lane == 0) {
+        const uint32_t a_base = q_lo + static_cast<uint32_t>((qb * S::kQBytes) >> 4);
+        const uint32_t b_base = k_lo + static_cast<uint32_t>((slot * S::kStageBytes) >> 4);
 #pragma unroll
         for (int kk = 0; kk < 4 * NB; ++kk) {
           if (kk < ksteps_qk) {
             const uint32_t a_off = static_cast<uint32_t>(((kk >> 2) * S::kTileBytes + (kk & 3) * 32) >> 4);
             const uint32_t b_off = static_cast<uint32_t>(((kk >> 2) * BN * 128 + (kk & 3) * 32) >> 4);
-            umma_f16_ss_w(tmem + buf * 128u, q_lo + a_off, kHi, b_lo + b_off, kHi, idesc_qk, kk > 0 ? 1u : 0u);
+            umma_f16_ss_w(tmem + buf * 128u, a_base + a_off, kHi, b_base + b_off, kHi, idesc_qk, kk > 0 ? 1u : 0u);
           }
         }
         umma_commit(&s_full[buf]);
-        umma_commit(&k_empty[st]);
-      };
-      // O_h += P_h V_h over keys [64 h, 64 h + 64): P_h from the first 32 columns of half h of S[buf], V rows
-      // from stage `st`.
-      auto pv = [&](uint32_t buf, int half, int st, bool first) {
-        const uint32_t b_lo = v_lo + static_cast<uint32_t>((st * S::kKVBytes) >> 4);
+      }
+    };
+    // O_h += P_h V_h over keys [64 h, 64 h + 64) for both halves: P_h from the first 32 columns of half h of
+    // S[buf], V rows from the stage of slot `slot`.
+    auto pv = [&](uint32_t buf, int slot, bool first) {
+      if (lane == 0) {
+        const uint32_t b_base = v_lo + static_cast<uint32_t>((slot * S::kStageBytes) >> 4);
 #pragma unroll
-        for (int k4 = 0; k4 < 4; ++k4) {
-          const int kk = 4 * half + k4;  // 16-key step within the tile
-          umma_f16_ts_w(tmem + S::o_col(half), tmem + buf * 128u + 64u * half + 8u * k4,
-                        b_lo + static_cast<uint32_t>((kk * 16 * 128) >> 4), kHi, idesc_pv,
-                        (!first || k4 > 0) ? 1u : 0u);
-        }
-        umma_commit(&pv_done[half]);
-      };
-      for (long long item = blockIdx.x; item < a.items; item += grid) {
-        HalvesItem c;
-        halves_item(a, item, c);
-        if (c.n <= 0) continue;
-        // prologue: S of the item's first two tiles
-        for (int j = 0; j < 2 && j < c.n; ++j) {
-          const int st = kc % NS;
-          if (wait_all_or_fail(j == 0 ? q_full : nullptr, qc & 1, &k_full[st], (kc / NS) & 1, nullptr, 0, 75 + j)) {
-            tc_fence_after_sync();
-            qk((g + j) & 1, st);
-          }
-          ++kc;
-        }
-        ++qc;
-        if (c.n <= 2 && ok) umma_commit(q_empty);  // every QK of this item is issued
-        for (int j = 0; j < c.n; ++j, ++g) {
-          const uint32_t buf = g & 1;
-          const int vst = vc % NS;
-          const uint32_t v_par = (vc / NS) & 1;
-          ++vc;
-          for (int half = 0; half < 2; ++half) {
-            // this half of P(j), the V tile (once) and, on an item's first tile, O read out by the epilogue
-            if (wait_all_or_fail(&p_full[half], pc & 1, half == 0 ? &v_full[vst] : nullptr, v_par,
-                                 (half == 0 && j == 0) ? o_empty : nullptr, (oc & 1) ^ 1, 77 + half)) {
-              tc_fence_after_sync();
-              pv(buf, half, vst, j == 0);
-            }
-          }
-          ++pc;
-          if (ok) umma_commit(&v_empty[vst]);
-          if (j + 2 < c.n) {
-            // both halves of P(j) are consumed (in issue order): S[buf] takes tile j + 2
-            const int st = kc % NS;
-            if (wait_all_or_fail(&k_full[st], (kc / NS) & 1, nullptr, 0, nullptr, 0, 79)) {
-              tc_fence_after_sync();
-              qk(buf, st);
-            }
-            ++kc;
-            if (j + 3 == c.n && ok) umma_commit(q_empty);
+        for (int half = 0; half < 2; ++half) {
+#pragma unroll
+          for (int k4 = 0; k4 < 4; ++k4) {
+            const int kk = 4 * half + k4;  // 16-key step within the tile
+            umma_f16_ts_w(tmem + S::o_col(half), tmem + buf * 128u + 64u * half + 8u * k4,
+                          b_base + static_cast<uint32_t>((kk * 16 * 128) >> 4), kHi, idesc_pv,
+                          (!first || k4 > 0) ? 1u : 0u);
           }
         }
-        ++oc;
+        umma_commit(pv_done);
       }
+    };
+    TileCursor cur, ahead;  // tile g and tile g + 2
+    tile_cursor_init(a, cur);
+    tile_cursor_init(a, ahead);
+    // prologue: S of the first two tiles
+    uint32_t g = 0;
+    for (int u = 0; u < 2 && ahead.valid; ++u) {
+      const int qb = (ahead.items_seen - 1) & 1;
+      if (ahead.j == 0) wait_lane0(&q_full[qb], ((ahead.items_seen - 1) >> 1) & 1, 75);
+      wait_lane0(&full[u], 0, 76 + u);
       if (ok) {
-        umma_commit(mma_done);
-        mbar_wait(mma_done, 0, a.budget_ns);
+        tc_fence_after_sync();
+        qk(u, qb, u);
+        if (lane == 0 && ahead.j + 1 == ahead.c.n) umma_commit(&q_empty[qb]);
       }
+      tile_cursor_advance(a, ahead);
     }
+    while (cur.valid) {
+      const uint32_t buf = g & 1;
+      const uint32_t u = g + 2;  // the stage holding V(g) and K(g + 2)
+      const int slot = u & 1;
+      __syncwarp();
+      named_barrier_sync(S::kBarP + buf, S::kBarPThreads);  // both halves of P(g) are in TMEM
+      wait_lane0(&full[slot], (u >> 1) & 1, 78);
+      if (ok) {
+        tc_fence_after_sync();
+        pv(buf, slot, cur.j == 0);
+        if (lane == 0 && cur.j + 1 == cur.c.n) umma_commit(o_full);  // the item's O is complete
+      }
+      if (ahead.valid) {
+        // S[buf] takes tile g + 2 (both halves of P(g) are consumed first, in issue order)
+        const int qb = (ahead.items_seen - 1) & 1;
+        if (ahead.j == 0) wait_lane0(&q_full[qb], ((ahead.items_seen - 1) >> 1) & 1, 79);
+        if (ok) {
+          tc_fence_after_sync();
+          qk(buf, qb, slot);
+          if (lane == 0 && ahead.j + 1 == ahead.c.n) umma_commit(&q_empty[qb]);  // every QK of that item issued
+        }
+        tile_cursor_advance(a, ahead);
+      }
+      tile_cursor_advance(a, cur);
+      ++g;
+    }
+    if (lane == 0 && ok) {
+      umma_commit(mma_done);
+      mbar_wait(mma_done, 0, a.budget_ns);
+    }
+    __syncwarp();
   } else if (warp >= 4) {
     // ------------------------------------------------------------------------- softmax / epilogue
     // Warpgroup 1 (warps 4-7) owns keys [0, 64) of every tile, warpgroup 2 (warps 8-11) keys [64, 128). A warp
@@ -327,7 +390,7 @@ __global__ void __launch_bounds__(384, 1)
     const uint32_t lane_base = static_cast<uint32_t>((warp % 4) * 32) << 16;
     const uint32_t o_own = tmem + lane_base + S::o_col(half);
     bool ok = true;
-    uint32_t g = 0, pvc = 0, vbase = 0;
+    uint32_t g = 0, items_done = 0;
     auto wait_warp = [&](uint64_t* bar, uint32_t parity, int site) {
       if (ok) {
         ok = __all_sync(0xffffffffu, mbar_wait(bar, parity, a.budget_ns));
@@ -335,7 +398,7 @@ __global__ void __launch_bounds__(384, 1)
       }
       return ok;
     };
-    for (long long item = blockIdx.x; item < a.items; item += grid) {
+    for (long long item = blockIdx.x; item < a.items; item += gridDim.x) {
       HalvesItem c;
       halves_item(a, item, c);
       const int q = c.q0 + row;
@@ -393,12 +456,10 @@ __global__ void __launch_bounds__(384, 1)
           halves_exp2_pack<Tr>(sr, make_float2(a.scale_log2, a.scale_log2), make_float2(neg_m, neg_m), acc, packed);
           tmem_st32(s_addr, packed);
         }
-        // O_h may be rescaled only once PV_h(j - 1) has completed. The wait happens on every tile, so this
-        // warpgroup is never more than one phase behind the barrier.
-        if (j > 0) {
-          wait_warp(&pv_done[half], pvc & 1, 82 + half);
-          ++pvc;
-          if (warp_grow && ok) {
+        // O_h may be rescaled only once PV(g - 1) has completed (at most that PV is outstanding here).
+        if (warp_grow && j > 0) {
+          wait_warp(pv_done, (g - 1) & 1, 82 + half);
+          if (ok) {
             tc_fence_after_sync();
             for (int cb = 0; cb < D / 16; ++cb) {
               uint32_t r[16];
@@ -410,14 +471,14 @@ __global__ void __launch_bounds__(384, 1)
             }
           }
         }
-        // Value rows past the cache end: this half's rows are zeroed before its P is released (PV_h reads them).
+        // Value rows past the cache end: this half's rows of V(g) are zeroed before its P is released (PV reads
+        // them). V(g) is in the stage u = g + 2.
         if (tok0 + BN > c.len) {
-          const uint32_t vcount = vbase + j;
-          const int vst = vcount % NS;
-          wait_warp(&v_full[vst], (vcount / NS) & 1, 84 + half);
+          const uint32_t u = g + 2;
+          wait_warp(&full[u & 1], (u >> 1) & 1, 84 + half);
           const int vrow = 64 * half + row;
           if (ok && row < 64 && tok0 + vrow >= c.len) {
-            uint8_t* dst = v_smem + vst * S::kKVBytes + vrow * 128;
+            uint8_t* dst = st_smem + (u & 1) * S::kStageBytes + vrow * 128;
 #pragma unroll
             for (int blk = 0; blk < NB; ++blk) {
 #pragma unroll
@@ -431,22 +492,22 @@ __global__ void __launch_bounds__(384, 1)
         if (ok) tmem_wait_st();
         tc_fence_before_sync();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&p_full[half]);
+        named_barrier_arrive(S::kBarP + buf, S::kBarPThreads);  // every tile, whatever happened above
         const float rowsum = (acc[0].x + acc[0].y) + (acc[1].x + acc[1].y) + (acc[2].x + acc[2].y) +
                              (acc[3].x + acc[3].y);
         l = l * alpha + rowsum;
         m = m_new;
       }
       if (c.n > 0) {
-        vbase += c.n;
-        wait_warp(&pv_done[half], pvc & 1, 86 + half);  // PV_h of the item's last tile
-        ++pvc;
+        wait_warp(o_full, items_done & 1, 86 + half);  // the item's last PV has completed
+        ++items_done;
       }
       // epilogue: merge the two halves' running states (LSE weights), then each warpgroup normalises and
       // stores alternate 16-column blocks of the row
       xch[(2 * half) * 128 + row] = m;
       xch[(2 * half + 1) * 128 + row] = l;
-      named_barrier_sync(2, 256);  // both halves' states, and both PV_h of the last tile, are complete
+      __syncwarp();  // the named barriers are the aligned form: the warp arrives converged
+      named_barrier_sync(S::kBarX, 256);  // both halves' states are published
       const float m0 = xch[row], l0 = xch[128 + row], m1 = xch[256 + row], l1 = xch[384 + row];
       const float mt = fmaxf(m0, m1);
       const float w0 = (m0 == -INFINITY) ? 0.f : fast_exp2(m0 - mt);
@@ -455,39 +516,47 @@ __global__ void __launch_bounds__(384, 1)
       const float inv = lt > 0.f ? 1.f / lt : 0.f;
       const float lse = (c.n > 0 && lt > 0.f) ? mt + fast_log2(lt) : kEmptyLse;
       const long long row_id = row_valid ? ((long long)c.b * a.sq + q) * a.heads + c.h : 0;
-      if (c.n > 0 && ok) tc_fence_after_sync();
-      for (int cb = half; cb < D / 16; cb += 2) {
-        float o[16];
-        if (c.n > 0 && ok) {  // warp-collective: every lane, valid row or not
-          uint32_t r0[16], r1[16];
-          tmem_ld16(tmem + lane_base + S::o_col(0) + cb * 16, r0);
-          tmem_ld16(tmem + lane_base + S::o_col(1) + cb * 16, r1);
-          tmem_wait_ld();
+      const bool read_o = c.n > 0 && ok;
+      if (read_o) tc_fence_after_sync();
+      // this warpgroup's blocks cb = half, half + 2, ...: both O halves of up to four blocks loaded before one wait
+      constexpr int kBlocks = NB * 4;  // 16-column blocks of the O accumulators (D / 16 of them hold data)
 #pragma unroll
-          for (int i = 0; i < 16; ++i) o[i] = (__uint_as_float(r0[i]) * w0 + __uint_as_float(r1[i]) * w1) * inv;
-        } else {
+      for (int c0 = 0; c0 < kBlocks; c0 += 4) {
+        uint32_t r0[2][16], r1[2][16];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) o[i] = 0.f;
+        for (int k = 0; k < 2; ++k) {
+          const int cb = c0 + 2 * k + half;
+          if (read_o && cb < D / 16) {  // warp-collective: every lane, valid row or not
+            tmem_ld16(tmem + lane_base + S::o_col(0) + cb * 16, r0[k]);
+            tmem_ld16(tmem + lane_base + S::o_col(1) + cb * 16, r1[k]);
+          }
         }
-        if (row_valid && a.write_partials) {
-          float4* dst = reinterpret_cast<float4*>(a.part_o + (row_id * a.splits + c.s) * D + cb * 16);
+        if (read_o) tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 4; ++i) dst[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
-        } else if (row_valid) {
-          uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<T*>(a.out) + row_id * D + cb * 16);
-          dst[0] = make_uint4(Tr::pack2(o[0], o[1]), Tr::pack2(o[2], o[3]), Tr::pack2(o[4], o[5]),
-                              Tr::pack2(o[6], o[7]));
-          dst[1] = make_uint4(Tr::pack2(o[8], o[9]), Tr::pack2(o[10], o[11]), Tr::pack2(o[12], o[13]),
-                              Tr::pack2(o[14], o[15]));
+        for (int k = 0; k < 2; ++k) {
+          const int cb = c0 + 2 * k + half;
+          if (cb >= D / 16) continue;
+          float o[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            o[i] = read_o ? (__uint_as_float(r0[k][i]) * w0 + __uint_as_float(r1[k][i]) * w1) * inv : 0.f;
+          }
+          if (row_valid && a.write_partials) {
+            float4* dst = reinterpret_cast<float4*>(a.part_o + (row_id * a.splits + c.s) * D + cb * 16);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) dst[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+          } else if (row_valid) {
+            uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<T*>(a.out) + row_id * D + cb * 16);
+            dst[0] = make_uint4(Tr::pack2(o[0], o[1]), Tr::pack2(o[2], o[3]), Tr::pack2(o[4], o[5]),
+                                Tr::pack2(o[6], o[7]));
+            dst[1] = make_uint4(Tr::pack2(o[8], o[9]), Tr::pack2(o[10], o[11]), Tr::pack2(o[12], o[13]),
+                                Tr::pack2(o[14], o[15]));
+          }
         }
       }
       if (row_valid && a.write_partials && half == 0) a.part_lse[row_id * a.splits + c.s] = lse;
-      named_barrier_sync(2, 256);  // the exchange slots are free for the next item
-      if (c.n > 0) {
-        tc_fence_before_sync();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(o_empty);
-      }
+      __syncwarp();
+      named_barrier_sync(S::kBarX, 256);  // the exchange slots are free for the next item
     }
   }
   tc_fence_before_sync();

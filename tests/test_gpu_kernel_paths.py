@@ -32,6 +32,18 @@ def test_kernel_path_matches_reference_golden(entry, path):
     _check(_run(inputs, path=path), expected, inputs)
 
 
+@pytest.mark.parametrize("kernel", ["halves", "single"])
+@pytest.mark.parametrize("entry", ENTRIES, ids=[e["key"] for e in ENTRIES])
+def test_other_tensor_kernels_match_reference_golden(entry, kernel):
+    # The key-halves kernel (head dims up to 128) and the one-tile kernel (every head dim) on every golden case.
+    case, seed, dtype, causal, pattern = entry_params(entry)
+    if kernel == "halves" and case[4] > 128:
+        pytest.skip("the key-halves kernel serves head dims up to 128")
+    inputs = build_case(case, seed, dtype, causal, pattern)
+    expected = dtype_bits_to_f32(expected_bits(entry), dtype_name(dtype))
+    _check(_run(inputs, path="tensor", tensor_kernel=kernel), expected, inputs)
+
+
 @pytest.mark.parametrize("entry", ENTRIES, ids=[e["key"] for e in ENTRIES])
 def test_tensor_strided_schedule_matches_reference_golden(entry):
     # the default (contiguous, pieces merged in-kernel) is covered above; whole items, strided, here
@@ -104,19 +116,26 @@ def test_decode_contiguous_schedule_pieces_merge_to_the_oracle(schedule, causal,
 SPLIT_ENTRIES = [e for e in ENTRIES if e["seed"] == 7 and e["pattern"] == "mixed"]
 
 
+@pytest.mark.parametrize("kernel", ["auto", "halves"])
 @pytest.mark.parametrize("splits", [2, 8])
 @pytest.mark.parametrize("entry", SPLIT_ENTRIES, ids=[e["key"] for e in SPLIT_ENTRIES])
-def test_tensor_path_splits_match_oracle(entry, splits):
+def test_tensor_path_splits_match_oracle(entry, splits, kernel):
     case, seed, dtype, causal, pattern = entry_params(entry)
     if splits > (case[5] * case[6] + 31) // 32:
         pytest.skip("more splits than 32-token tiles in table capacity")
+    if kernel == "halves" and case[4] > 128:
+        pytest.skip("the key-halves kernel serves head dims up to 128")
     inputs = build_case(case, seed, dtype, causal, pattern)
-    _check(_run(inputs, path="tensor", cube_mode="general", num_splits=splits), oracle_output(inputs), inputs)
+    _check(_run(inputs, path="tensor", cube_mode="general", num_splits=splits, tensor_kernel=kernel),
+           oracle_output(inputs), inputs)
 
 
+@pytest.mark.parametrize("kernel", ["auto", "halves"])
 @pytest.mark.parametrize("dim", [16, 48, 64, 80, 128, 144, 192, 256])
 @pytest.mark.parametrize("page", [16, 48, 64])
-def test_tensor_path_long_causal_tails(dim, page):
+def test_tensor_path_long_causal_tails(dim, page, kernel):
+    if kernel == "halves" and dim > 128:
+        pytest.skip("the key-halves kernel serves head dims up to 128")
     # Config-4 style: several 128-row query tiles, causal, ragged lengths incl. 0 and partial pages,
     # 1% of K rows scaled x8 to stress the running max.
     case = (f"edge_d{dim}_p{page}", 3, 200, 2, dim, page, (700 + page - 1) // page)
@@ -130,7 +149,7 @@ def test_tensor_path_long_causal_tails(dim, page):
     k, v = poison_unread(k, v, table, lengths, page)
     inputs = {"case": case, "seed": 2026, "dtype": torch.float16, "causal": True, "pattern": "edge", "q": q,
               "k": k, "v": v, "table": table, "lengths": torch.tensor(lengths, dtype=torch.int32)}
-    _check(_run(inputs, path="tensor"), oracle_output(inputs), inputs)
+    _check(_run(inputs, path="tensor", tensor_kernel=kernel), oracle_output(inputs), inputs)
 
 
 @pytest.mark.parametrize("case,splits,causal,pattern,dtype,programs", [
