@@ -480,6 +480,75 @@ def run_decode(args, rank, world, device, stream):
             "launches_per_step": len(fns), "steps": steps, "inp": inp, "out": out}
 
 
+def run_decode_serving(args, dc, rank, world, device, stream):
+    """Config 5 as a serving loop runs it: every step the cache lengths grow by one token (each request appends
+    one), the step's query rows and lengths are uploaded from pinned host memory, the forward goes through the
+    product API (mha_paged_decode_sharded: this rank's heads) with the host copy of the new lengths, and the
+    output is read back. The launcher is cached per shape and split count, so new lengths cost no rebuild;
+    ``host_us_per_call`` is the host time the API call itself takes (median), the rest is device time."""
+    from fgw_b200.operators.mha.sharded import mha_paged_decode_sharded
+    inp = dc["inp"]
+    steps = max(10, args.steps)
+    base = np.asarray(inp["host_lengths"], dtype=np.int64)
+    host_q = inp["q"].cpu().pin_memory()
+    host_len = torch.empty(base.shape[0], dtype=torch.int32).pin_memory()
+    host_out = torch.empty(inp["q"].shape, dtype=inp["q"].dtype).pin_memory()
+    dev_q, dev_len = torch.empty_like(inp["q"]), torch.empty_like(inp["lengths"])
+    out = torch.empty_like(inp["q"])
+    schedule = [np.maximum(base - (steps + 3 - i), 1) for i in range(steps + 3)]  # grows to the config's lengths
+    host_us, events = [], []
+    for i, lengths in enumerate(schedule):
+        host_len.numpy()[:] = lengths
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        dev_q.copy_(host_q, non_blocking=True)
+        dev_len.copy_(host_len, non_blocking=True)
+        t0 = time.perf_counter()
+        mha_paged_decode_sharded(dev_q, inp["k"], inp["v"], inp["table"], dev_len, inp["page"], shard="heads",
+                                 cache_lengths=lengths, out=out)
+        host_us.append((time.perf_counter() - t0) * 1e6)
+        host_out.copy_(out, non_blocking=True)
+        e1.record(stream)
+        events.append((e0, e1))
+    torch.cuda.synchronize()
+    step_ms = [a.elapsed_time(b) for a, b in events][3:]  # the first three are warm-up
+    live = [int(x.sum()) for x in schedule[3:]]
+    nbytes = statistics.mean(live) * inp["heads"] * DECODE["dim"] * 2 * 2
+    return {"step_ms": statistics.median(step_ms), "host_us": statistics.median(host_us[3:]),
+            "host_us_max": max(host_us[3:]), "bytes": nbytes, "steps": steps,
+            "h2d": host_q.numel() * host_q.element_size() + host_len.numel() * 4,
+            "d2h": host_out.numel() * host_out.element_size()}
+
+
+def run_longq_strong(args, rank, world, device, stream):
+    """Config 2 strong-scaled: the one B2 H8 call sharded by head over the ranks through the product API
+    (mha_paged_decode_sharded), each rank H/N heads of both requests; timed without and with the gathered output
+    (one all-gather). Eager steps with the L2 flushed, device time per rank, max over ranks."""
+    from fgw_b200.operators.mha.sharded import head_shard, mha_paged_decode_sharded
+    c = LONGQ
+    first, count = head_shard(c["heads"], rank, world)
+    inp = longq_inputs(1000, device)  # the same call on every rank: rank r keeps its heads
+    heads = slice(first, first + count)
+    q = inp["q"][:, :, heads].contiguous()
+    k, v = inp["k"][:, heads].contiguous(), inp["v"][:, heads].contiguous()
+    a = (q, k, v, inp["table"], inp["lengths"], c["page"])
+    kw = dict(shard="heads", cache_lengths=inp["host_lengths"], tensor_kernel=args.tensor_kernel)
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=device)
+    result = {}
+    for name, gather in (("local", False), ("gathered", True)):
+        fn = (lambda g=gather: mha_paged_decode_sharded(*a, gather=g, **kw))
+        barrier(world)
+        per, totals = timed_steps([(name, fn)], max(5, args.steps // 2), 3, flush, stream)
+        barrier(world)
+        result[name + "_ms"] = statistics.median(totals)
+    out = mha_paged_decode_sharded(*a, gather=True, **kw)
+    torch.cuda.synchronize()
+    ok = check_longq(inp, out)  # the assembled output against a PyTorch FP32 reference
+    flops = flops_of(inp, c["sq"], c["heads"], c["dim"])
+    return {**result, "flops": flops, "parity": ok, "heads_per_rank": count,
+            "launches": 2 * 2 * max(5, args.steps // 2)}  # plan + attend per call, both variants
+
+
 def run_gather(args, dc, device, stream):
     """Paged-cache gather of K and V over the config-5 pool into packed dense buffers, then the decode attention
     over the packed copy (identity page table, original lengths), against the direct decode's output."""
@@ -800,6 +869,20 @@ def main(argv=None):
             "l2": "flushed (256 MiB write) before every step; eager plan + attend, per-stage events",
             "parity": lq32["parity"], "gpu_launches": lq32["launches"]}
         line["gpu_launches"] = line.get("gpu_launches", 0) + lq32["launches"]
+    if args.only is None:
+        st = run_longq_strong(args, rank, world, device, stream)
+        local_ms = max_over_ranks(st["local_ms"], world)
+        gathered_ms = max_over_ranks(st["gathered_ms"], world)
+        line["longq_strong"] = {
+            "workload": "longq_b2h8_q4096_kv2048_bf16_d128_page128", "scaling": "strong",
+            "parallelism": f"head-shard x{world} ({st['heads_per_rank']} heads per GPU)",
+            "us_per_call": local_ms * 1e3, "unit": "TFLOP/s", "value": st["flops"] / (local_ms * 1e-3) / 1e12,
+            "gathered_us_per_call": gathered_ms * 1e3,
+            "gathered_value": st["flops"] / (gathered_ms * 1e-3) / 1e12,
+            "how": "mha_paged_decode_sharded per rank (eager, L2 flushed, median step, max over ranks); gathered = "
+                   "plus one all-gather assembling O[B,Sq,H,D] on every rank",
+            "parity": st["parity"], "gpu_launches": st["launches"]}
+        line["gpu_launches"] = line.get("gpu_launches", 0) + st["launches"]
     if not args.no_decode and args.only in (None, "decode"):
         dc = run_decode(args, rank, world, device, stream)
         step_ms = max_over_ranks(dc["step_ms"], world)
@@ -818,6 +901,18 @@ def main(argv=None):
                   "num_splits": k.num_splits, "parity": dc["parity"],
                   "gpu_launches": dc["launches_per_step"] * dc["steps"],
                   "stage_ms": {n: statistics.mean(v) for n, v in dc["per"].items()}}
+        sv = run_decode_serving(args, dc, rank, world, device, stream)
+        sv_ms = max_over_ranks(sv["step_ms"], world)
+        decode["serving"] = {
+            "how": "lengths grow by one token per step; per step: H2D of Q and lengths from pinned memory, "
+                   "mha_paged_decode_sharded with the host lengths, D2H of O; device time per step (median, max "
+                   "over ranks); host_us_per_call = host time of the API call",
+            "ms_per_step": sv_ms, "value": sum_over_ranks(sv["bytes"], world) / (sv_ms * 1e-3) / 1e9, "unit": "GB/s",
+            "host_us_per_call": max_over_ranks(sv["host_us"], world),
+            "host_us_per_call_max": max_over_ranks(sv["host_us_max"], world),
+            "h2d_bytes_per_step": sv["h2d"], "d2h_bytes_per_step": sv["d2h"], "steps": sv["steps"],
+            "gpu_launches": 2 * sv["steps"]}
+        decode["gpu_launches"] += 2 * sv["steps"]
         line["decode"] = decode
         line["gpu_launches"] = line.get("gpu_launches", 0) + decode["gpu_launches"]
         if not args.no_gather:
