@@ -225,9 +225,10 @@ __device__ __forceinline__ float fast_exp2(float x) {
 
 // 2^x for a pair on the FMA pipe instead of the SFU, for x in [-127, 2^22): Cody-Waite style range
 // reduction x = n + f with n = round(x), f in [-0.5, 0.5] (rounding by adding 1.5 * 2^23), then a
-// degree-3 polynomial for 2^f whose coefficients were fitted here by iteratively reweighted least
-// squares on the relative error (max relative error 7.5e-5 over [-0.5, 0.5], below half an FP16 ulp),
-// and 2^n applied by adding n to the exponent field. Inputs below -127 are clamped (result ~6e-39).
+// degree-3 polynomial for 2^f, and 2^n applied by adding n to the exponent field. Inputs below -127 are
+// clamped (result ~6e-39). The coefficients are the minimax fit of the relative error on [-0.5, 0.5] that
+// fit_exp2_poly.py (beside this header) computes by Lawson's iteratively reweighted least squares; max
+// relative error 7.5e-5, below half an FP16 ulp.
 __device__ __forceinline__ float2 poly_exp2_pair(float2 x) {
   const float2 magic = make_float2(12582912.0f, 12582912.0f);
   x.x = fmaxf(x.x, -127.0f);
@@ -235,10 +236,10 @@ __device__ __forceinline__ float2 poly_exp2_pair(float2 x) {
   const float2 t = __fadd2_rn(x, magic);                                  // n in the low mantissa bits
   const float2 n = __fadd2_rn(t, make_float2(-12582912.0f, -12582912.0f));
   const float2 f = __fadd2_rn(x, make_float2(-n.x, -n.y));
-  float2 p = make_float2(0.0551716648042202f, 0.0551716648042202f);
-  p = __ffma2_rn(p, f, make_float2(0.2426111251115799f, 0.2426111251115799f));
-  p = __ffma2_rn(p, f, make_float2(0.6932609677314758f, 0.6932609677314758f));
-  p = __ffma2_rn(p, f, make_float2(0.9999280571937561f, 0.9999280571937561f));
+  float2 p = make_float2(0.0551713221f, 0.0551713221f);
+  p = __ffma2_rn(p, f, make_float2(0.242610544f, 0.242610544f));
+  p = __ffma2_rn(p, f, make_float2(0.693260968f, 0.693260968f));
+  p = __ffma2_rn(p, f, make_float2(0.999928117f, 0.999928117f));
   // (bits(t) << 23) == (n << 23) mod 2^32, since bits(t) = 0x4B400000 + n.
   const int bx = __float_as_int(p.x) + (__float_as_int(t.x) << 23);
   const int by = __float_as_int(p.y) + (__float_as_int(t.y) << 23);
