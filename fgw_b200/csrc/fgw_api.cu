@@ -40,32 +40,33 @@ long long pair_items(const fgw_mha_params& p) {
   return static_cast<long long>(p.batch) * p.heads * p.num_splits * ((p.q_len + kPairRows - 1) / kPairRows);
 }
 
-long long stream_items(const fgw_mha_params& p) {
-  if (resolve_path(p) == FGW_PATH_DECODE) {
-    const int rows = decode_rows_per_item(p.head_dim);
-    return static_cast<long long>(p.batch) * ((p.q_len + rows - 1) / rows) * p.heads * p.num_splits;
-  }
-  return pair_items(p);
+int stream_slot_rows(const fgw_mha_params& p) {
+  if (resolve_path(p) == FGW_PATH_DECODE) return decode_rows_per_item(p.head_dim);
+  return resolve_tensor_kernel(p) == FGW_TENSOR_KERNEL_HALVES ? 128 : kPairRows;
 }
 
-int stream_slot_rows(const fgw_mha_params& p) {
-  return resolve_path(p) == FGW_PATH_DECODE ? decode_rows_per_item(p.head_dim) : kPairRows;
+long long stream_items(const fgw_mha_params& p) {
+  const int rows = stream_slot_rows(p);
+  return static_cast<long long>(p.batch) * ((p.q_len + rows - 1) / rows) * p.heads * p.num_splits;
 }
 
 // Decode path, one split: the contiguous schedule unless STRIDED is asked for. Its cut gives every CTA the same
 // number of KV stages whatever the spread of cache lengths (whole items dealt round-robin leave the CTAs that
 // drew the longest requests as stragglers when there are few items per CTA), and costs two piece partials per
 // CTA at most.
-// Tensor path: AUTO takes the contiguous schedule only when whole items would leave more than a third of the
-// programs idle in their single wave (items < 2/3 of the programs): measured on config 2 (256 items, 148
-// programs, two waves) the strided schedule is faster, since cutting items adds segment starts and piece
-// merges.
+// Tensor path, key-halves kernel: the contiguous schedule (S double-buffering starts a segment's first QKs during
+// the previous segment, so cuts are cheap). Two-tile kernel: AUTO takes the contiguous schedule only when whole
+// items would leave more than a third of the programs idle in their single wave (items < 2/3 of the programs):
+// measured on config 2 (256 items, 148 programs, two waves) the strided schedule is faster there, since cutting
+// items adds segment starts and piece merges.
 bool use_stream_schedule(const fgw_mha_params& p) {
   if (p.schedule == FGW_SCHEDULE_STRIDED || p.num_splits != 1) return false;
   if (stream_items(p) > kStreamMaxItems) return false;
   if (resolve_path(p) == FGW_PATH_DECODE) return true;
-  const bool applies = p.head_dim <= 128 && resolve_tensor_kernel(p) == FGW_TENSOR_KERNEL_PAIRS;
-  if (!applies) return false;
+  if (p.head_dim > 128) return false;
+  const int kernel = resolve_tensor_kernel(p);
+  if (kernel == FGW_TENSOR_KERNEL_HALVES) return true;
+  if (kernel != FGW_TENSOR_KERNEL_PAIRS) return false;
   return p.schedule == FGW_SCHEDULE_CONTIGUOUS || p.schedule == FGW_SCHEDULE_TAIL ||
          3 * pair_items(p) < 2ll * kStreamMaxPrograms;
 }

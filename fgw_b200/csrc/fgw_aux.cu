@@ -24,7 +24,9 @@ constexpr int kPlanSortMax = 8192;
 // max(KV tiles, 1) units; program p gets units [p * (total / G) + min(p, total % G), ...) as in the
 // reference's balanced plan (static_schedule.py:64-66).
 struct StreamPlanArgs {
-  int enabled, items, programs, heads, sq, causal, qpairs;
+  // tensor path: items of `block_rows` query rows (256: the two-tile kernel, 128: the key-halves kernel),
+  // `qblocks` of them per (request, head)
+  int enabled, items, programs, heads, sq, causal, qblocks, block_rows;
   // decode path (decode != 0): items are (request, query-row block, head) with `rows` query rows each and
   // `tile`-token KV units (the decode kernel's stage), `row_blocks` blocks per request
   int decode, rows, tile, row_blocks;
@@ -36,8 +38,8 @@ struct StreamPlanArgs {
   int32_t* counters;
 };
 
-// Units of work item `item` (KV tiles seen by its last query row; at least 1): the two-tile kernel's
-// item decomposition with one split (pair_item in fgw_fmha2_sm100.cu).
+// Units of work item `item` (KV tiles seen by its last query row; at least 1): the tensor kernels' item
+// decomposition with one split (pair_item in fgw_fmha2_sm100.cu, halves_item in fgw_fmha_halves_sm100.cu).
 __device__ __forceinline__ long long stream_item_units(const StreamPlanArgs& s, const int32_t* lens,
                                                        const int32_t* order, int item) {
   if (s.decode) {
@@ -49,10 +51,10 @@ __device__ __forceinline__ long long stream_item_units(const StreamPlanArgs& s, 
     const int visible = s.causal ? max(len - s.sq + last + 1, 0) : len;
     return max((visible + s.tile - 1) / s.tile, 1);
   }
-  const int p_rev = item % s.qpairs;
-  const int b = order[(item / s.qpairs) / s.heads];
-  const int q0 = (s.qpairs - 1 - p_rev) * 256;
-  const int last = min(q0 + 256, s.sq) - 1;
+  const int p_rev = item % s.qblocks;
+  const int b = order[(item / s.qblocks) / s.heads];
+  const int q0 = (s.qblocks - 1 - p_rev) * s.block_rows;
+  const int last = min(q0 + s.block_rows, s.sq) - 1;
   const int len = lens[b];
   const int visible = s.causal ? max(len - s.sq + last + 1, 0) : len;
   return max((visible + 127) / 128, 1);
@@ -183,7 +185,8 @@ cudaError_t launch_plan(const LaunchDesc& d) {
     sp.heads = d.p.heads;
     sp.sq = d.p.q_len;
     sp.causal = d.p.causal;
-    sp.qpairs = (d.p.q_len + kPairRows - 1) / kPairRows;
+    sp.block_rows = d.slot_rows;  // one work item's query rows
+    sp.qblocks = (d.p.q_len + sp.block_rows - 1) / sp.block_rows;
     if (resolve_path(d.p) == FGW_PATH_DECODE) {
       sp.decode = 1;
       sp.rows = decode_rows_per_item(d.p.head_dim);

@@ -44,6 +44,15 @@ struct HalvesArgs {
   WorkspaceHeader* ws;
   int batch, sq, heads, dim, width, page, splits, causal, box_rows, write_partials, qtiles;
   long long items;
+  // contiguous schedule (one split): per-program first item, unit offset and first unit, the per-item arrival
+  // counters and two partial slots of 128 rows per program; whole items below tail_start first
+  int contiguous, programs, tail_start;
+  const int32_t* prog_item;
+  const int32_t* prog_off;
+  const long long* prog_u;
+  int32_t* counters;
+  float* slot_lse;
+  float* slot_o;
   float scale_log2;
   uint64_t budget_ns;
 };
@@ -101,13 +110,73 @@ __device__ __forceinline__ void halves_item(const HalvesArgs& a, long long item,
   c.n = static_cast<int>((long long)tiles * (c.s + 1) / a.splits) - c.n_begin;
 }
 
-// Walks the CTA's non-empty items tile by tile, `ahead` tiles ahead of a consumer: the producer and the MMA warp
-// need the item of tile g + 2 while they work on tile g.
+// One run of KV tiles of one item processed by this CTA: a whole item, or, with the contiguous schedule, tiles
+// [first, first + count) of an item (a piece when other CTAs hold the rest of it).
+struct HalvesSegment {
+  long long item;
+  bool piece;
+  long long item_u;  // first unit of the item in the contiguous cut
+  int units;         // units of the whole item (at least 1)
+};
+
+struct SegmentWalk {
+  long long whole;  // next whole item (strided part)
+  long long item;
+  int off;
+  long long u, u_end;
+};
+
+__device__ __forceinline__ void segment_walk_init(const HalvesArgs& a, SegmentWalk& k) {
+  k.whole = blockIdx.x;
+  k.item = a.contiguous ? a.prog_item[blockIdx.x] : 0;
+  k.off = a.contiguous ? a.prog_off[blockIdx.x] : 0;
+  k.u = a.contiguous ? a.prog_u[blockIdx.x] : 0;
+  k.u_end = a.contiguous ? a.prog_u[blockIdx.x + 1] : 0;
+}
+
+// The next segment of this CTA, with `c` the item restricted to the segment's tiles. Every role walks the same
+// segments in the same order: whole items first (all of them with the strided schedule), then the CTA's
+// contiguous range of units.
+__device__ __forceinline__ bool segment_walk_next(const HalvesArgs& a, SegmentWalk& k, HalvesSegment& sg,
+                                                  HalvesItem& c) {
+  const long long whole_end = a.contiguous ? a.tail_start : a.items;
+  if (k.whole < whole_end) {
+    sg.item = k.whole;
+    sg.piece = false;
+    sg.item_u = 0;
+    sg.units = 0;
+    halves_item(a, k.whole, c);
+    k.whole += gridDim.x;
+    return true;
+  }
+  if (!a.contiguous || k.u >= k.u_end) return false;
+  halves_item(a, k.item, c);  // one split: the whole item
+  const int tiles = c.n;
+  const int units = max(tiles, 1);  // an item without keys still costs one unit (its rows are written as zeros)
+  const int count = static_cast<int>(min(static_cast<long long>(units - k.off), k.u_end - k.u));
+  sg.item = k.item;
+  sg.piece = count < units;
+  sg.item_u = k.u - k.off;
+  sg.units = units;
+  c.n_begin = k.off;
+  c.n = max(0, min(k.off + count, tiles) - k.off);
+  k.u += count;
+  k.off += count;
+  if (k.off >= units) {
+    ++k.item;
+    k.off = 0;
+  }
+  return true;
+}
+
+// Walks the CTA's segments that have tiles, tile by tile, `ahead` tiles ahead of a consumer: the producer and the
+// MMA warp need the segment of tile g + 2 while they work on tile g.
 struct TileCursor {
-  long long next_item;  // next item to look at
-  HalvesItem c;         // current item
-  int j;                // tile within it
-  int items_seen;       // non-empty items entered so far (their Q buffer is (items_seen - 1) % 2)
+  SegmentWalk walk;
+  HalvesSegment sg;
+  HalvesItem c;    // current segment's item, restricted to its tiles
+  int j;           // tile within it
+  int items_seen;  // segments with tiles entered so far (their Q buffer is (items_seen - 1) % 2)
   bool valid;
 };
 
@@ -117,9 +186,7 @@ __device__ __forceinline__ void tile_cursor_advance(const HalvesArgs& a, TileCur
     return;
   }
   t.valid = false;
-  while (t.next_item < a.items) {
-    halves_item(a, t.next_item, t.c);
-    t.next_item += gridDim.x;
+  while (segment_walk_next(a, t.walk, t.sg, t.c)) {
     if (t.c.n > 0) {
       t.j = 0;
       ++t.items_seen;
@@ -130,7 +197,7 @@ __device__ __forceinline__ void tile_cursor_advance(const HalvesArgs& a, TileCur
 }
 
 __device__ __forceinline__ void tile_cursor_init(const HalvesArgs& a, TileCursor& t) {
-  t.next_item = blockIdx.x;
+  segment_walk_init(a, t.walk);
   t.j = 0;
   t.items_seen = 0;
   t.valid = false;
@@ -398,9 +465,12 @@ __global__ void __launch_bounds__(384, 1)
       }
       return ok;
     };
-    for (long long item = blockIdx.x; item < a.items; item += gridDim.x) {
-      HalvesItem c;
-      halves_item(a, item, c);
+    SegmentWalk walk;
+    segment_walk_init(a, walk);
+    HalvesSegment sg;
+    HalvesItem c;
+    volatile int* merge_flag = reinterpret_cast<volatile int*>(smem + S::kTmemSlot + 4);
+    while (segment_walk_next(a, walk, sg, c)) {
       const int q = c.q0 + row;
       const bool row_valid = q < a.sq;
       const int vis = row_valid ? halves_visible(q, c.len, a.sq, a.causal) : 0;
@@ -516,6 +586,14 @@ __global__ void __launch_bounds__(384, 1)
       const float inv = lt > 0.f ? 1.f / lt : 0.f;
       const float lse = (c.n > 0 && lt > 0.f) ? mt + fast_log2(lt) : kEmptyLse;
       const long long row_id = row_valid ? ((long long)c.b * a.sq + q) * a.heads + c.h : 0;
+      long long my_slot = 0;  // this program's slot for a piece (contiguous schedule)
+      if (sg.piece) {
+        const long long total = a.prog_u[a.programs];
+        const int q_first = program_of(total, a.programs, sg.item_u);
+        const int first_extra = sg.item_u != program_start(total, a.programs, q_first) ? 1 : 0;
+        my_slot = piece_slot(q_first, first_extra, static_cast<int>(blockIdx.x) - q_first);
+        if (row_valid && half == 0) a.slot_lse[my_slot * 128 + row] = lse;
+      }
       const bool read_o = c.n > 0 && ok;
       if (read_o) tc_fence_after_sync();
       // this warpgroup's blocks cb = half, half + 2, ...: both O halves of up to four blocks loaded before one wait
@@ -541,7 +619,11 @@ __global__ void __launch_bounds__(384, 1)
           for (int i = 0; i < 16; ++i) {
             o[i] = read_o ? (__uint_as_float(r0[k][i]) * w0 + __uint_as_float(r1[k][i]) * w1) * inv : 0.f;
           }
-          if (row_valid && a.write_partials) {
+          if (row_valid && sg.piece) {
+            float4* dst = reinterpret_cast<float4*>(a.slot_o + (my_slot * 128 + row) * D + cb * 16);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) dst[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+          } else if (row_valid && a.write_partials) {
             float4* dst = reinterpret_cast<float4*>(a.part_o + (row_id * a.splits + c.s) * D + cb * 16);
 #pragma unroll
             for (int i = 0; i < 4; ++i) dst[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
@@ -555,8 +637,72 @@ __global__ void __launch_bounds__(384, 1)
         }
       }
       if (row_valid && a.write_partials && half == 0) a.part_lse[row_id * a.splits + c.s] = lse;
+      if (sg.piece) {
+        // A piece of an item cut between CTAs: its partial (normalised FP32 O and base-2 LSE) went to this
+        // program's slot above; it counts itself in on the item's counter, and the piece whose arrival completes
+        // the set merges every piece from its slot in piece order (so the result does not depend on which CTA
+        // finished last). No CTA waits for another.
+        __threadfence();
+        __syncwarp();
+        named_barrier_sync(S::kBarX, 256);  // both warpgroups have written their blocks
+        if (warp == 4 && lane == 0) {
+          const long long total = a.prog_u[a.programs];
+          const int q_first = program_of(total, a.programs, sg.item_u);
+          const int pieces = program_of(total, a.programs, sg.item_u + sg.units - 1) - q_first + 1;
+          *merge_flag = atomicAdd(&a.counters[sg.item], 1) + 1 == pieces ? 1 : 0;
+        }
+        __syncwarp();
+        named_barrier_sync(S::kBarX, 256);
+        const int merge = *merge_flag;
+        if (merge) {
+          __threadfence();
+          if (warp == 4 && lane == 0) a.counters[sg.item] = 0;  // ready for the next launch
+        }
+        if (merge && row_valid) {
+          const long long total = a.prog_u[a.programs];
+          const int q_first = program_of(total, a.programs, sg.item_u);
+          const int pieces = program_of(total, a.programs, sg.item_u + sg.units - 1) - q_first + 1;
+          const int first_extra = sg.item_u != program_start(total, a.programs, q_first) ? 1 : 0;
+          float peak = kEmptyLse;
+          for (int k = 0; k < pieces; ++k) {
+            peak = fmaxf(peak, __ldcg(&a.slot_lse[piece_slot(q_first, first_extra, k) * 128 + row]));
+          }
+          float wsum = 0.f;
+          for (int k = 0; k < pieces; ++k) {
+            const float lk = __ldcg(&a.slot_lse[piece_slot(q_first, first_extra, k) * 128 + row]);
+            if (lk > kValidLse) wsum += fast_exp2(lk - peak);
+          }
+          const float scale = wsum > 0.f ? 1.f / wsum : 0.f;
+          for (int cb = half; cb < D / 16; cb += 2) {
+            float acc[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) acc[i] = 0.f;
+            for (int k = 0; k < pieces; ++k) {
+              const long long pr = piece_slot(q_first, first_extra, k) * 128 + row;
+              const float lk = __ldcg(&a.slot_lse[pr]);
+              if (!(lk > kValidLse)) continue;
+              const float w = fast_exp2(lk - peak);
+              const float4* src = reinterpret_cast<const float4*>(a.slot_o + pr * D + cb * 16);
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const float4 v = __ldcg(src + i);
+                acc[4 * i] += w * v.x;
+                acc[4 * i + 1] += w * v.y;
+                acc[4 * i + 2] += w * v.z;
+                acc[4 * i + 3] += w * v.w;
+              }
+            }
+            uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<T*>(a.out) + row_id * D + cb * 16);
+            dst[0] = make_uint4(Tr::pack2(acc[0] * scale, acc[1] * scale), Tr::pack2(acc[2] * scale, acc[3] * scale),
+                                Tr::pack2(acc[4] * scale, acc[5] * scale), Tr::pack2(acc[6] * scale, acc[7] * scale));
+            dst[1] = make_uint4(Tr::pack2(acc[8] * scale, acc[9] * scale), Tr::pack2(acc[10] * scale, acc[11] * scale),
+                                Tr::pack2(acc[12] * scale, acc[13] * scale),
+                                Tr::pack2(acc[14] * scale, acc[15] * scale));
+          }
+        }
+      }
       __syncwarp();
-      named_barrier_sync(S::kBarX, 256);  // the exchange slots are free for the next item
+      named_barrier_sync(S::kBarX, 256);  // the exchange slots and the merge flag are free for the next segment
     }
   }
   tc_fence_before_sync();
@@ -582,7 +728,9 @@ static cudaError_t launch_halves_t(const LaunchDesc& d, const HalvesArgs& args, 
   err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kBytes);
   if (err != cudaSuccess) return err;
   const long long cap = d.p.grid_cap > 0 ? d.p.grid_cap : d.sm_count;
-  const long long grid = std::min<long long>(args.items, std::min<long long>(cap, d.sm_count));
+  // contiguous schedule: one CTA per program of the plan; strided: persistent CTAs over the items
+  const long long grid = args.contiguous ? args.programs
+                                         : std::min<long long>(args.items, std::min<long long>(cap, d.sm_count));
   if (grid <= 0) return cudaSuccess;
   kernel<<<(unsigned)grid, S::kThreads, S::kBytes, d.stream>>>(qmap, kmap, vmap, args);
   return cudaGetLastError();
@@ -613,6 +761,15 @@ cudaError_t launch_tensor_halves(const LaunchDesc& d, bool write_partials, const
   args.items = (long long)p.batch * p.heads * p.num_splits * args.qtiles;
   args.scale_log2 = (1.0f / sqrtf((float)p.head_dim)) * kLog2e;
   args.budget_ns = d.budget_ns;
+  args.contiguous = d.contiguous ? 1 : 0;
+  args.programs = d.contiguous ? d.programs : 0;
+  args.tail_start = d.contiguous ? d.tail_start : 0;
+  args.prog_item = d.prog_item;
+  args.prog_off = d.prog_off;
+  args.prog_u = d.prog_u;
+  args.counters = d.counters;
+  args.slot_lse = d.slot_lse;
+  args.slot_o = d.slot_o;
   const bool bf16 = p.dtype == FGW_DTYPE_BFLOAT16;
   if (p.head_dim <= 64) {
     return bf16 ? launch_halves_t<__nv_bfloat16, 1>(d, args, qmap, kmap, vmap)

@@ -77,10 +77,11 @@ typedef enum fgw_path {
  *   TAIL:       STRIDED for the full waves (the first floor(items / G) * G items, G = the programs), then
  *               CONTIGUOUS over the items of the last, partial wave only (the reference's tail plan,
  *               static_schedule.py:83-116 `make_tail_plan`): only those items are cut into pieces.
- *   AUTO:       decode path with one split: CONTIGUOUS. Tensor path: CONTIGUOUS where it applies and there are
- *               fewer work items than 2/3 of 148 programs (whole items would leave SMs idle), STRIDED otherwise.
- * CONTIGUOUS and TAIL apply with num_splits == 1 to the decode kernel and to the PAIRS tensor kernel; elsewhere
- * the launch runs STRIDED (fgw_mha_resolve_schedule reports which).
+ *   AUTO:       with one split: CONTIGUOUS on the decode path and for the HALVES tensor kernel; for the PAIRS
+ *               tensor kernel CONTIGUOUS only when there are fewer work items than 2/3 of 148 programs (whole
+ *               items would leave SMs idle), STRIDED otherwise.
+ * CONTIGUOUS and TAIL apply with num_splits == 1 to the decode kernel and to the PAIRS and HALVES tensor kernels;
+ * elsewhere the launch runs STRIDED (fgw_mha_resolve_schedule reports which).
  */
 typedef enum fgw_schedule {
   FGW_SCHEDULE_AUTO = 0,
@@ -94,7 +95,7 @@ typedef enum fgw_schedule {
  *   PAIRS:  two 128-row query tiles per work item sharing every K/V tile (head_dim <= 128).
  *   SINGLE: one 128-row query tile per work item, P through shared memory (any head_dim).
  *   HALVES: one query tile per work item, S double-buffered in TMEM, the softmax split by key halves over two
- *           warpgroups (head_dim <= 128, strided schedule only).
+ *           warpgroups (head_dim <= 128).
  * A kernel that cannot serve the head_dim returns FGW_ERR_UNSUPPORTED. */
 typedef enum fgw_tensor_kernel {
   FGW_TENSOR_KERNEL_AUTO = 0,

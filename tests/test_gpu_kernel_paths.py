@@ -53,12 +53,13 @@ def test_tensor_strided_schedule_matches_reference_golden(entry):
     _check(_run(inputs, path="tensor", task_assignment="strided"), expected, inputs)
 
 
+@pytest.mark.parametrize("kernel", ["auto", "halves"])
 @pytest.mark.parametrize("schedule,causal,programs",
                          [("contiguous", False, 1), ("contiguous", False, 3), ("contiguous", False, 7),
                           ("contiguous", False, None), ("contiguous", True, 28), ("contiguous", True, None),
                           ("tail", False, 1), ("tail", False, 4), ("tail", False, 5), ("tail", False, 7),
                           ("tail", False, None), ("tail", True, 28)])
-def test_contiguous_schedule_pieces_merge_to_the_oracle(schedule, causal, programs):
+def test_contiguous_schedule_pieces_merge_to_the_oracle(schedule, causal, programs, kernel):
     # Few programs over many KV tiles: items are cut into pieces at arbitrary tile offsets, some items
     # span many programs, and the last arriver of each merges them in the same launch. (The reference's
     # general route, taken when causal, accepts only its default program caps.)
@@ -71,7 +72,7 @@ def test_contiguous_schedule_pieces_merge_to_the_oracle(schedule, causal, progra
               "k": k, "v": v, "table": table, "lengths": torch.tensor(lengths, dtype=torch.int32)}
     # 18 items (3 requests x 2 heads x 3 query pairs): the tail schedule deals floor(18 / G) * G whole items
     # strided and cuts only the rest (none with one program, all of them with 148)
-    kwargs = dict(path="tensor", task_assignment=schedule)
+    kwargs = dict(path="tensor", task_assignment=schedule, tensor_kernel=kernel)
     if programs is not None:
         kwargs["persistent_programs"] = programs
     out = _run(inputs, **kwargs)

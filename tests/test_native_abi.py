@@ -169,11 +169,18 @@ def test_resolved_schedule_per_path_and_kernel():
     slots = 2 * 148 * 1 * (128 + 1) * 4  # D128 decode items carry one query row
     assert (_native.workspace_size(_params(**decode))
             >= _native.workspace_size(_params(schedule=_native.SCHEDULE_STRIDED, **decode)) + slots)
-    # tensor path: the two-tile kernel takes the contiguous cut; the single-tile and key-halves kernels do not
+    # tensor path: the two-tile and key-halves kernels take the contiguous cut (the key-halves kernel on AUTO, with
+    # 128-row slots); the one-tile kernel does not
     tensor = dict(q_len=4096, num_splits=1, path=_native.PATH_TENSOR, schedule=_native.SCHEDULE_CONTIGUOUS)
     assert _native.resolve_schedule(_params(**tensor)) == _native.SCHEDULE_CONTIGUOUS
-    for kernel in (_native.TENSOR_KERNEL_SINGLE, _native.TENSOR_KERNEL_HALVES):
-        assert _native.resolve_schedule(_params(tensor_kernel=kernel, **tensor)) == _native.SCHEDULE_STRIDED
+    halves = dict(tensor, schedule=_native.SCHEDULE_AUTO, tensor_kernel=_native.TENSOR_KERNEL_HALVES, batch=8,
+                  heads=16)
+    assert _native.resolve_schedule(_params(**halves)) == _native.SCHEDULE_CONTIGUOUS
+    assert (_native.workspace_size(_params(**halves))
+            >= _native.workspace_size(_params(**dict(halves, schedule=_native.SCHEDULE_STRIDED)))
+            + 2 * 148 * 128 * (128 + 1) * 4)
+    assert _native.resolve_schedule(_params(tensor_kernel=_native.TENSOR_KERNEL_SINGLE, **tensor)) == \
+        _native.SCHEDULE_STRIDED
     with pytest.raises(_native.FgwError):
         _native.check(_native.library().fgw_mha_paged_fwd(ctypes.byref(_params(tensor_kernel=4)), None, 0, None),
                       "fgw_mha_paged_fwd")
