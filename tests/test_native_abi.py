@@ -162,13 +162,14 @@ def test_resolved_schedule_per_path_and_kernel():
     # decode path with one split: the contiguous cut (slots of the decode kernel's query rows); with splits, or
     # when STRIDED is asked for, whole items
     decode = dict(batch=256, heads=32, q_len=1, num_splits=1, path=_native.PATH_DECODE)
-    assert _native.resolve_schedule(_params(**decode)) == _native.SCHEDULE_CONTIGUOUS
+    assert _native.resolve_schedule(_params(**decode)) == _native.SCHEDULE_STRIDED  # AUTO
+    contiguous = dict(decode, schedule=_native.SCHEDULE_CONTIGUOUS)
+    assert _native.resolve_schedule(_params(**contiguous)) == _native.SCHEDULE_CONTIGUOUS
     assert _native.resolve_schedule(_params(**dict(decode, num_splits=2))) == _native.SCHEDULE_STRIDED
     assert _native.resolve_schedule(_params(schedule=_native.SCHEDULE_STRIDED, **decode)) == _native.SCHEDULE_STRIDED
     assert _native.resolve_schedule(_params(schedule=_native.SCHEDULE_TAIL, **decode)) == _native.SCHEDULE_TAIL
     slots = 2 * 148 * 1 * (128 + 1) * 4  # D128 decode items carry one query row
-    assert (_native.workspace_size(_params(**decode))
-            >= _native.workspace_size(_params(schedule=_native.SCHEDULE_STRIDED, **decode)) + slots)
+    assert _native.workspace_size(_params(**contiguous)) >= _native.workspace_size(_params(**decode)) + slots
     # tensor path: the two-tile and key-halves kernels take the contiguous cut (the key-halves kernel on AUTO, with
     # 128-row slots); the one-tile kernel does not
     tensor = dict(q_len=4096, num_splits=1, path=_native.PATH_TENSOR, schedule=_native.SCHEDULE_CONTIGUOUS)
