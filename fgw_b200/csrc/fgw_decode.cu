@@ -113,19 +113,32 @@ __device__ __forceinline__ int decode_units(const DecodeArgs& a, long long item)
   return max((visible + S::kTile - 1) / S::kTile, 1);
 }
 
+template <bool kContiguous>
 __device__ __forceinline__ void decode_cursor_init(const DecodeArgs& a, DecodeCursor& k) {
   k.whole = blockIdx.x;
-  k.item = a.contiguous ? a.prog_item[blockIdx.x] : 0;
-  k.off = a.contiguous ? a.prog_off[blockIdx.x] : 0;
-  k.u = a.contiguous ? a.prog_u[blockIdx.x] : 0;
-  k.u_end = a.contiguous ? a.prog_u[blockIdx.x + 1] : 0;
+  k.item = kContiguous ? a.prog_item[blockIdx.x] : 0;
+  k.off = kContiguous ? a.prog_off[blockIdx.x] : 0;
+  k.u = kContiguous ? a.prog_u[blockIdx.x] : 0;
+  k.u_end = kContiguous ? a.prog_u[blockIdx.x + 1] : 0;
 }
 
 // The producer and the consumers walk the same segments in the same order: whole items first (all of them
-// with the strided schedule), then the CTA's contiguous range of units.
-template <int D>
+// with the strided schedule), then the CTA's contiguous range of units. The schedule is a template parameter, so
+// the strided kernel carries none of the contiguous schedule's state (the consumers run at the register limit).
+template <int D, bool kContiguous>
 __device__ __forceinline__ bool decode_next(const DecodeArgs& a, DecodeCursor& k, DecodeSegment& sg) {
-  const long long whole_end = a.contiguous ? a.tail_start : a.items;
+  if (!kContiguous) {
+    if (k.whole >= a.items) return false;
+    sg.item = k.whole;
+    sg.first = 0;
+    sg.count = -1;
+    sg.piece = false;
+    sg.item_u = 0;
+    sg.units = 0;
+    k.whole += gridDim.x;
+    return true;
+  }
+  const long long whole_end = a.tail_start;
   if (k.whole < whole_end) {
     sg.item = k.whole;
     sg.first = 0;
@@ -136,7 +149,7 @@ __device__ __forceinline__ bool decode_next(const DecodeArgs& a, DecodeCursor& k
     k.whole += gridDim.x;
     return true;
   }
-  if (!a.contiguous || k.u >= k.u_end) return false;
+  if (k.u >= k.u_end) return false;
   const int units = decode_units<D>(a, k.item);
   const int count = static_cast<int>(min(static_cast<long long>(units - k.off), k.u_end - k.u));
   sg.item = k.item;
@@ -166,7 +179,7 @@ __device__ __forceinline__ void segment_range(const DecodeSegment& sg, int tiles
   }
 }
 
-template <typename T, int D>
+template <typename T, int D, bool kContiguous>
 __global__ void __launch_bounds__(DecodeShape<D>::kThreads, 1)
     decode_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
                   const DecodeArgs a) {
@@ -205,9 +218,9 @@ __global__ void __launch_bounds__(DecodeShape<D>::kThreads, 1)
       const int boxes = S::kTile / a.box_rows;
       const uint32_t box_bytes = a.box_rows * D * sizeof(T);
       DecodeCursor cur;
-      decode_cursor_init(a, cur);
+      decode_cursor_init<kContiguous>(a, cur);
       DecodeSegment sg;
-      while (decode_next<D>(a, cur, sg)) {
+      while (decode_next<D, kContiguous>(a, cur, sg)) {
         int b, rb, s, h;
         decode_item(sg.item, a.heads, a.splits, a.row_blocks, a.order, b, rb, s, h);
         const int len = a.lengths[b];
@@ -260,9 +273,9 @@ __global__ void __launch_bounds__(DecodeShape<D>::kThreads, 1)
   uint32_t it = 0;
 
   DecodeCursor cur;
-  decode_cursor_init(a, cur);
+  decode_cursor_init<kContiguous>(a, cur);
   DecodeSegment sg;
-  while (decode_next<D>(a, cur, sg)) {
+  while (decode_next<D, kContiguous>(a, cur, sg)) {
     int b, rb, s, h;
     decode_item(sg.item, a.heads, a.splits, a.row_blocks, a.order, b, rb, s, h);
     const int len = a.lengths[b];
@@ -456,7 +469,7 @@ __global__ void __launch_bounds__(DecodeShape<D>::kThreads, 1)
     // A piece of an item cut between CTAs (contiguous schedule) writes its partial to its program's slot.
     long long my_slot = 0;
     int pieces = 1, q_first = 0, first_extra = 0;
-    if (sg.piece) {
+    if (kContiguous && sg.piece) {
       const long long total = a.prog_u[a.programs];
       q_first = program_of(total, a.programs, sg.item_u);
       pieces = program_of(total, a.programs, sg.item_u + sg.units - 1) - q_first + 1;
@@ -484,7 +497,7 @@ __global__ void __launch_bounds__(DecodeShape<D>::kThreads, 1)
       }
       const long long row_id = ((long long)b * a.sq + qi) * a.heads + h;
       const float val = den > 0.f ? num / den : 0.f;
-      if (sg.piece) {
+      if (kContiguous && sg.piece) {
         a.slot_o[(my_slot * kRows + r) * D + d] = val;
         if (d == 0) a.slot_lse[my_slot * kRows + r] = den > 0.f ? mx + fast_log2(den) : kEmptyLse;
       } else if (a.write_partials) {
@@ -494,7 +507,7 @@ __global__ void __launch_bounds__(DecodeShape<D>::kThreads, 1)
         reinterpret_cast<T*>(a.out)[row_id * D + d] = Tr::from_float(val);
       }
     }
-    if (sg.piece) {
+    if (kContiguous && sg.piece) {
       // Piece merge in place: every piece publishes its partial, then counts itself in on the item's counter;
       // the piece whose arrival completes the set merges all pieces from their slots in piece order (the split
       // merge's arithmetic), so the output does not depend on which CTA finished last. No CTA waits for another.
@@ -594,7 +607,7 @@ static cudaError_t launch_decode_t(const LaunchDesc& d, const DecodeArgs& args, 
                                    const CUtensorMap& vmap) {
   using S = DecodeShape<D>;
   using M = DecodeSmem<T, D>;
-  auto kernel = decode_kernel<T, D>;
+  auto kernel = args.contiguous ? decode_kernel<T, D, true> : decode_kernel<T, D, false>;
   cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, M::kBytes);
   if (err != cudaSuccess) return err;
   long long grid = args.items;

@@ -118,8 +118,10 @@ __device__ __forceinline__ void exp2_pack_half(const uint32_t* sr, float2 scale2
     } else {
       p = make_float2(fast_exp2(x.x), fast_exp2(x.y));
     }
-    acc[i % 4] = __fadd2_rn(acc[i % 4], p);
     packed[i] = Tr::pack2(p.x, p.y);
+    // the row sum adds the rounded values PV multiplies: with the lazily rescaled running max a row's largest P
+    // may exceed 1 and round, and normalising by the unrounded sum would leave that rounding in the output
+    acc[i % 4] = __fadd2_rn(acc[i % 4], Tr::unpack2(packed[i]));
   }
 }
 

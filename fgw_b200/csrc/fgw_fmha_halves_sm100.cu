@@ -3,30 +3,30 @@
 //
 // Same contract, masking rules and epilogues as the other tensor kernels; the reference body it stands for is
 // operators/mha/kernels/mha_paged_decode_ascend_v7.py:225-315, 375-465. The schedule:
-//   * one 128-row query tile per work item (request, head, split, query tile); the CTA's items form one global
-//     sequence of KV tiles g = 0, 1, ...; S is double-buffered in TMEM (S[g % 2]), so QK(g + 2) is issued right
-//     after PV(g) and the softmax of tile g + 1 never waits for the tensor core;
-//   * two softmax warpgroups: warps 4-7 own keys [0, 64) of every 128-key tile, warps 8-11 keys [64, 128). Each
-//     keeps its own running max and sum and its own O accumulator (O_0, O_1 in TMEM), like two interleaved KV
-//     splits, so the warpgroups never exchange a row max inside the loop; the epilogue merges the two halves
-//     with their LSE weights;
-//   * P of each half goes back into the first 32 TMEM columns of that half of S, and PV_h reads it from there
-//     (tcgen05.mma with the A operand in tensor memory);
-//   * one shared-memory stage per tile holds V(g) and K(g + 2) (stage u = g + 2 holds V(u - 2) and K(u); the first
-//     two stages of the sequence hold K only), so the MMA warp waits on one barrier per tile, and a stage is free
-//     once QK(u) has completed (the commit that publishes S also releases the stage: QK(u) is issued after
-//     PV(u - 2));
-//   * the softmax warps hand P(g) to the MMA warp through a named barrier (bar.arrive / bar.sync) instead of an
-//     mbarrier the issuing thread polls; the MMA warp runs as a whole warp, one lane issuing;
-//   * Q is double-buffered, so the next item's first two QKs run while this item's epilogue reads O.
-// TMEM: S0 [0, 128), S1 [128, 256), O_0 [256, 256 + D), O_1 [384, 384 + D) of 512 columns.
+//   * one 128-row query tile per work item (request, head, split, query tile); the CTA's segments (whole items,
+//     or pieces of items under the contiguous schedule) form one sequence of KV tiles g = 0, 1, ...; S is
+//     double-buffered in TMEM (S[g % 2]), so QK(g + 2) is issued right after PV(g) and the softmax of tile g + 1
+//     never waits for the tensor core;
+//   * Q lives in TMEM (two buffers: the next segment's Q is written while this one runs) and both products read
+//     their A operand from TMEM (tcgen05.mma with A in tensor memory): only K and V come from shared memory. A
+//     QK with Q in shared memory reads 8 KB of operands per M128 N128 K16 instruction, more than shared memory
+//     delivers in the instruction's 64 cycles (measured on B200: ~116 cycles each); with Q in TMEM it reads 4 KB;
+//   * two softmax warpgroups: warps 4-7 own keys [0, 64) of every 128-key tile, warps 8-11 keys [64, 128). They
+//     exchange their partial row maxima through shared memory once per tile, so both halves exponentiate against
+//     the same running max and accumulate into one O; each keeps its own partial row sum;
+//   * P of each half goes back into the first 32 TMEM columns of that half of S, and PV reads it from there;
+//   * K and V have rings of their own (K(g) is free once QK(g) has completed, V(g) once PV(g) has), so a tile's
+//     loads start two tile periods before they are needed;
+//   * the softmax warps hand P(g) to the MMA warp through a named barrier (bar.arrive / bar.sync); the MMA warp
+//     runs as a whole warp, one lane issuing.
+// TMEM: S0 [0, 128), S1 [128, 256), O [256, 256 + D), Q0 [384, 384 + D / 2), Q1 [448, 448 + D / 2).
 //
 // Barrier phases. Every parity wait below is on a phase that cannot be two completions old: s_full[b] completes
-// once per QK into S[b], and QK(g + 2) needs P(g), which its waiters have not released yet; pv_done completes
-// once per tile and a softmax warp that rescales at tile g + 1 has seen S(g + 1), whose QK was issued after
-// PV(g - 1), so at most PV(g) is outstanding; o_full completes once per non-empty item and the next item's last
-// PV needs this item's epilogue first; full[s] completes once per stage and stage u + 2 reuses the slot only
-// after QK(u). The producer waits on s_full for a stage's release, which needs exactly two stages in the ring.
+// once per QK into S[b], and QK(g + 2) needs P(g), which its waiters have not released yet; pv_done completes once
+// per tile and a softmax warp that rescales at tile g + 1 has seen S(g + 1), whose QK was issued after PV(g - 1),
+// so at most PV(g) is outstanding; o_full completes once per segment with tiles and the next segment's last PV
+// needs this segment's epilogue first; a ring's full barrier of slot s is reloaded only after the tile it holds
+// has been consumed; q_ready[b] / q_free[b] alternate with the segments.
 #include <algorithm>
 
 #include "fgw_common.cuh"
@@ -35,6 +35,7 @@
 namespace fgw {
 
 struct HalvesArgs {
+  const void* q;
   void* out;
   const int32_t* table;
   const int32_t* lengths;
@@ -59,29 +60,28 @@ struct HalvesArgs {
 
 template <int NB>
 struct HalvesShape {
-  static constexpr int kBN = 128;                  // keys per KV tile; each softmax warpgroup owns 64
-  static constexpr int kTileBytes = 128 * 128;     // one 64-column block of a 128-row operand
-  static constexpr int kQBytes = NB * kTileBytes;  // one query tile
-  static constexpr int kKBytes = NB * kBN * 128;   // one K (or V) tile
-  static constexpr int kStageBytes = 2 * kKBytes;  // V(u - 2) at 0, K(u) at kKBytes
-  static constexpr int kStages = 2;                // the s_full release needs exactly two (see above)
+  static constexpr int kBN = 128;                    // keys per KV tile; each softmax warpgroup owns 64
+  static constexpr int kTileBytes = NB * kBN * 128;  // one K (or V) tile: NB 64-column blocks of 128 rows
+  static constexpr int kStages = NB == 1 ? 6 : 3;    // per ring
   static constexpr int kThreads = 384;
   // registers per thread after the warpgroup split (4 x 32 x 88 + 8 x 32 x 208 = 384 x 168)
   static constexpr int kRegsControl = 88;
   static constexpr int kRegsSoftmax = 208;
-  __device__ __forceinline__ static uint32_t o_col(int h) { return 256u + 128u * static_cast<uint32_t>(h); }
+  static constexpr uint32_t kColO = 256;
+  __device__ __forceinline__ static uint32_t q_col(int b) { return 384u + 64u * static_cast<uint32_t>(b); }
   static constexpr int kTmemCols = 512;
-  // shared memory carve-up; kX: per half, the row max and row sum of every row, for the epilogue merge
-  static constexpr int kQ = 0;
-  static constexpr int kStage = kQ + 2 * kQBytes;
-  static constexpr int kX = kStage + kStages * kStageBytes;
-  static constexpr int kBar = kX + 2 * 2 * 128 * 4;
-  // q_full[2], q_empty[2], full[kStages], s_full[2], pv_done, o_full, mma_done
-  static constexpr int kNumBars = 4 + kStages + 5;
+  // shared memory: K ring, V ring, the partial row maxima of both halves (two tiles' worth) and row sums
+  static constexpr int kK = 0;
+  static constexpr int kV = kK + kStages * kTileBytes;
+  static constexpr int kXMax = kV + kStages * kTileBytes;  // [2 tiles][2 halves][128 rows] float
+  static constexpr int kXSum = kXMax + 2 * 2 * 128 * 4;    // [2 halves][128 rows] float
+  static constexpr int kBar = kXSum + 2 * 128 * 4;
+  // k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2], q_ready[2], q_free[2], pv_done, o_full, mma_done
+  static constexpr int kNumBars = 4 * kStages + 9;
   static constexpr int kTmemSlot = kBar + kNumBars * 8;
   static constexpr int kBytes = kTmemSlot + 16 + 1024;
   // named barriers: P(g) handed over on kBarP + g % 2 (8 softmax warps arrive, the MMA warp syncs); the two
-  // warpgroups exchange their epilogue states on kBarX
+  // warpgroups exchange row maxima and sums on kBarX
   static constexpr uint32_t kBarP = 4;
   static constexpr uint32_t kBarPThreads = 9 * 32;
   static constexpr uint32_t kBarX = 6;
@@ -169,14 +169,14 @@ __device__ __forceinline__ bool segment_walk_next(const HalvesArgs& a, SegmentWa
   return true;
 }
 
-// Walks the CTA's segments that have tiles, tile by tile, `ahead` tiles ahead of a consumer: the producer and the
-// MMA warp need the segment of tile g + 2 while they work on tile g.
+// Walks the CTA's segments that have tiles, tile by tile: the producer and the MMA warp keep one cursor on the
+// tile they consume and one two tiles ahead.
 struct TileCursor {
   SegmentWalk walk;
   HalvesSegment sg;
-  HalvesItem c;    // current segment's item, restricted to its tiles
-  int j;           // tile within it
-  int items_seen;  // segments with tiles entered so far (their Q buffer is (items_seen - 1) % 2)
+  HalvesItem c;  // current segment's item, restricted to its tiles
+  int j;         // tile within it
+  int seg;       // index of the current segment among those with tiles (its Q buffer is seg % 2)
   bool valid;
 };
 
@@ -189,7 +189,7 @@ __device__ __forceinline__ void tile_cursor_advance(const HalvesArgs& a, TileCur
   while (segment_walk_next(a, t.walk, t.sg, t.c)) {
     if (t.c.n > 0) {
       t.j = 0;
-      ++t.items_seen;
+      ++t.seg;
       t.valid = true;
       return;
     }
@@ -199,13 +199,13 @@ __device__ __forceinline__ void tile_cursor_advance(const HalvesArgs& a, TileCur
 __device__ __forceinline__ void tile_cursor_init(const HalvesArgs& a, TileCursor& t) {
   segment_walk_init(a, t.walk);
   t.j = 0;
-  t.items_seen = 0;
+  t.seg = -1;
   t.valid = false;
   tile_cursor_advance(a, t);
 }
 
 // 2^(s * scale - m) for the 64 scores of one half row (32 FP32 pairs, scale-and-subtract two lanes per
-// instruction), summed into four partial sums and packed to 16-bit pairs.
+// instruction), packed to 16-bit pairs and summed, as rounded, into four partial sums.
 template <typename Tr>
 __device__ __forceinline__ void halves_exp2_pack(const uint32_t (&sr)[64], float2 scale2, float2 negm2,
                                                  float2 (&acc)[4], uint32_t (&packed)[32]) {
@@ -213,9 +213,10 @@ __device__ __forceinline__ void halves_exp2_pack(const uint32_t (&sr)[64], float
   for (int i = 0; i < 32; ++i) {
     const float2 x = __ffma2_rn(make_float2(__uint_as_float(sr[2 * i]), __uint_as_float(sr[2 * i + 1])), scale2,
                                 negm2);
-    const float2 p = make_float2(fast_exp2(x.x), fast_exp2(x.y));
-    acc[i % 4] = __fadd2_rn(acc[i % 4], p);
-    packed[i] = Tr::pack2(p.x, p.y);
+    packed[i] = Tr::pack2(fast_exp2(x.x), fast_exp2(x.y));
+    // the row sum adds the rounded values PV multiplies (with the lazily rescaled running max a row's largest P
+    // may exceed 1 and round; normalising by the unrounded sum would leave that rounding in the output)
+    acc[i % 4] = __fadd2_rn(acc[i % 4], Tr::unpack2(packed[i]));
   }
 }
 
@@ -225,36 +226,46 @@ __device__ __forceinline__ void named_barrier_arrive(uint32_t id, uint32_t threa
 
 template <typename T, int NB>
 __global__ void __launch_bounds__(384, 1)
-    fmha_halves_sm100_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
-                             const __grid_constant__ CUtensorMap vmap, const HalvesArgs a) {
+    fmha_halves_sm100_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
+                             const HalvesArgs a) {
   using S = HalvesShape<NB>;
   using Tr = ElemTraits<T>;
   constexpr int BN = S::kBN;
+  constexpr int NS = S::kStages;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* q_smem = smem + S::kQ;
-  uint8_t* st_smem = smem + S::kStage;
-  float* xch = reinterpret_cast<float*>(smem + S::kX);  // [half][0: max, 1: sum][row]
+  uint8_t* k_smem = smem + S::kK;
+  uint8_t* v_smem = smem + S::kV;
+  float* xmax = reinterpret_cast<float*>(smem + S::kXMax);  // [tile parity][half][row]
+  float* xsum = reinterpret_cast<float*>(smem + S::kXSum);  // [half][row]
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::kBar);
-  uint64_t* q_full = bars + 0;        // [2]
-  uint64_t* q_empty = bars + 2;       // [2]
-  uint64_t* full = bars + 4;          // [kStages]: a stage's V and K have landed
-  uint64_t* s_full = full + S::kStages;  // [2]: S[b] holds a tile's scores (and frees the stage of that QK)
-  uint64_t* pv_done = s_full + 2;     // PV of a tile has completed
-  uint64_t* o_full = pv_done + 1;     // the last PV of an item has completed
+  uint64_t* k_full = bars;
+  uint64_t* k_empty = k_full + NS;
+  uint64_t* v_full = k_empty + NS;
+  uint64_t* v_empty = v_full + NS;
+  uint64_t* s_full = v_empty + NS;  // [2]: S[b] holds a tile's scores
+  uint64_t* q_ready = s_full + 2;   // [2]: Q buffer b holds the segment's query tile
+  uint64_t* q_free = q_ready + 2;   // [2]: every QK reading Q buffer b has completed
+  uint64_t* pv_done = q_free + 2;   // PV of a tile has completed
+  uint64_t* o_full = pv_done + 1;   // the last PV of a segment has completed
   uint64_t* mma_done = o_full + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::kTmemSlot);
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&q_full[i], 1);
-      mbar_init(&q_empty[i], 1);
-      mbar_init(&s_full[i], 1);
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
     }
-    for (int i = 0; i < S::kStages; ++i) mbar_init(&full[i], 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&q_ready[i], 8);  // every softmax warp writes its rows' half of Q
+      mbar_init(&q_free[i], 1);
+    }
     mbar_init(pv_done, 1);
     mbar_init(o_full, 1);
     mbar_init(mma_done, 1);
@@ -273,76 +284,57 @@ __global__ void __launch_bounds__(384, 1)
   if (warp < 4) setmaxnreg_dec<S::kRegsControl>();  // warpgroup 0: TMA, MMA and two idle warps
   if (warp == 0) {
     // ------------------------------------------------------------------------- TMA producer
-    // Stage u (ring slot u % 2) holds V(u - 2) and K(u) of the CTA's tile sequence; Q of each item goes into Q
-    // buffer (item % 2) just before the item's first K.
+    // K(t) into K-ring slot t % NS, V(t) into V-ring slot t % NS, in the order K0, K1, V0, K2, V1, K3, ...: the
+    // order the MMA warp consumes them (QK(g + 2) follows PV(g)).
     if (lane == 0) {
-      tma_prefetch_desc(&qmap);
       tma_prefetch_desc(&kmap);
       tma_prefetch_desc(&vmap);
       bool ok = true;
       const int boxes = BN / a.box_rows;
       const uint32_t box_bytes = a.box_rows * 128;
-      auto fail = [&](int site) {
-        ok = false;
-        record_error(a.ws, FGW_ERR_DEVICE_TIMEOUT, site);
-      };
-      // the live boxes of tile j of item c, and their loads into dst
-      auto live_boxes = [&](const HalvesItem& c, int j) {
+      auto load = [&](const CUtensorMap* map, const HalvesItem& c, int j, uint8_t* ring, uint64_t* full,
+                      uint64_t* empty, uint32_t t, int site) {
+        const int slot = t % NS;
+        if (ok && !mbar_wait(&empty[slot], ((t / NS) & 1) ^ 1, a.budget_ns)) {
+          ok = false;
+          record_error(a.ws, FGW_ERR_DEVICE_TIMEOUT, site);
+        }
+        if (!ok) return;
         const int tok0 = (c.n_begin + j) * BN;
         int nbox = 0;
         for (int k = 0; k < boxes; ++k) nbox += (tok0 + k * a.box_rows < c.len) ? 1 : 0;
-        return nbox;
-      };
-      auto load_tile = [&](const CUtensorMap* map, const HalvesItem& c, int j, uint8_t* dst, uint64_t* bar,
-                           int nbox) {
+        mbar_arrive_expect_tx(&full[slot], NB * nbox * box_bytes);
+        uint8_t* dst = ring + slot * S::kTileBytes;
         const int32_t* row_table = a.table + (long long)c.b * a.width;
-        const int tok0 = (c.n_begin + j) * BN;
         for (int k = 0; k < nbox; ++k) {
           const int tok = tok0 + k * a.box_rows;
           const int row = row_table[tok / a.page] * a.page + tok % a.page;
           for (int blk = 0; blk < NB; ++blk) {
-            tma_load_3d(dst + blk * BN * 128 + k * box_bytes, map, bar, blk * 64, c.h, row);
+            tma_load_3d(dst + blk * BN * 128 + k * box_bytes, map, &full[slot], blk * 64, c.h, row);
           }
         }
       };
-      TileCursor kc, vc;  // K(u) and V(u - 2)
+      TileCursor kc, vc;
       tile_cursor_init(a, kc);
       tile_cursor_init(a, vc);
-      uint32_t u = 0;
-      while (kc.valid || vc.valid) {
-        const int slot = u & 1;
-        // the slot's previous stage (u - 2) is free once QK(u - 2) has completed
-        if (ok && u >= 2 && !mbar_wait(&s_full[slot], ((u - 2) >> 1) & 1, a.budget_ns)) fail(70);
-        const bool has_k = kc.valid;
-        const bool has_v = u >= 2 && vc.valid;
-        if (has_k && kc.j == 0) {
-          // the item's Q, into buffer (items - 1) % 2, once the item two back has issued its last QK
-          const int qb = (kc.items_seen - 1) & 1;
-          if (ok && kc.items_seen > 2 && !mbar_wait(&q_empty[qb], ((kc.items_seen - 3) >> 1) & 1, a.budget_ns)) {
-            fail(71);
-          }
-          if (ok) {
-            mbar_arrive_expect_tx(&q_full[qb], S::kQBytes);
-            for (int blk = 0; blk < NB; ++blk) {
-              tma_load_4d(q_smem + qb * S::kQBytes + blk * S::kTileBytes, &qmap, &q_full[qb], blk * 64, kc.c.h,
-                          kc.c.q0, kc.c.b);
-            }
-          }
-        }
-        const int kbox = has_k ? live_boxes(kc.c, kc.j) : 0;
-        const int vbox = has_v ? live_boxes(vc.c, vc.j) : 0;
-        if (ok) {
-          uint8_t* dst = st_smem + slot * S::kStageBytes;
-          mbar_arrive_expect_tx(&full[slot], NB * (kbox + vbox) * box_bytes);
-          if (has_v) load_tile(&vmap, vc.c, vc.j, dst, &full[slot], vbox);
-          if (has_k) load_tile(&kmap, kc.c, kc.j, dst + S::kKBytes, &full[slot], kbox);
-        }
-        if (has_k) tile_cursor_advance(a, kc);
-        if (has_v) tile_cursor_advance(a, vc);
-        ++u;
+      uint32_t kt = 0, vt = 0;
+      for (int i = 0; i < 2 && kc.valid; ++i, ++kt) {
+        load(&kmap, kc.c, kc.j, k_smem, k_full, k_empty, kt, 70);
+        tile_cursor_advance(a, kc);
       }
-      // leave no copy in flight: the last two stages landed (or their waits gave up)
-      for (uint32_t w = (u >= 2 ? u - 2 : 0); w < u; ++w) mbar_wait(&full[w & 1], (w >> 1) & 1, a.budget_ns);
+      while (vc.valid) {
+        load(&vmap, vc.c, vc.j, v_smem, v_full, v_empty, vt, 71);
+        tile_cursor_advance(a, vc);
+        ++vt;
+        if (kc.valid) {
+          load(&kmap, kc.c, kc.j, k_smem, k_full, k_empty, kt, 72);
+          tile_cursor_advance(a, kc);
+          ++kt;
+        }
+      }
+      // leave no copy in flight: the last loads of both rings landed (or their waits gave up)
+      for (uint32_t t = (kt > NS ? kt - NS : 0); t < kt; ++t) mbar_wait(&k_full[t % NS], (t / NS) & 1, a.budget_ns);
+      for (uint32_t t = (vt > NS ? vt - NS : 0); t < vt; ++t) mbar_wait(&v_full[t % NS], (t / NS) & 1, a.budget_ns);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------------- UMMA issuer (whole warp, lane 0
@@ -351,9 +343,8 @@ __global__ void __launch_bounds__(384, 1)
     const int fmt = Tr::kUmmaFormat;
     const uint32_t idesc_qk = umma_idesc_f16(fmt, 128, BN, 0, 0);
     const uint32_t idesc_pv = umma_idesc_f16(fmt, 128, D, 0, 1);
-    const uint32_t q_lo = umma_desc_lo(smem_u32(q_smem), 16);
-    const uint32_t k_lo = umma_desc_lo(smem_u32(st_smem + S::kKBytes), 16);
-    const uint32_t v_lo = umma_desc_lo(smem_u32(st_smem), BN * 128);
+    const uint32_t k_lo = umma_desc_lo(smem_u32(k_smem), 16);
+    const uint32_t v_lo = umma_desc_lo(smem_u32(v_smem), BN * 128);
     constexpr uint32_t kHi = umma_desc_hi(1024, 2);
     const int ksteps_qk = D / 16;
     auto wait_lane0 = [&](uint64_t* bar, uint32_t parity, int site) {
@@ -365,80 +356,65 @@ __global__ void __launch_bounds__(384, 1)
       ok = __shfl_sync(0xffffffffu, ok && good, 0);
       return ok;
     };
-    // S[buf] = Q K^T with Q from buffer qb and K from the stage of slot `slot`; publishes S[buf] (and frees the
-    // stage for the producer).
+    // S[buf] = Q K^T with Q from TMEM buffer qb and K from ring slot `slot`; publishes S[buf], frees the K slot.
     auto qk = [&](uint32_t buf, int qb, int slot) {
       if (lane == 0) {
-        const uint32_t a_base = q_lo + static_cast<uint32_t>((qb * S::kQBytes) >> 4);
-        const uint32_t b_base = k_lo + static_cast<uint32_t>((slot * S::kStageBytes) >> 4);
+        const uint32_t b_base = k_lo + static_cast<uint32_t>((slot * S::kTileBytes) >> 4);
 #pragma unroll
         for (int kk = 0; kk < 4 * NB; ++kk) {
           if (kk < ksteps_qk) {
-            const uint32_t a_off = static_cast<uint32_t>(((kk >> 2) * S::kTileBytes + (kk & 3) * 32) >> 4);
             const uint32_t b_off = static_cast<uint32_t>(((kk >> 2) * BN * 128 + (kk & 3) * 32) >> 4);
-            umma_f16_ss_w(tmem + buf * 128u, a_base + a_off, kHi, b_base + b_off, kHi, idesc_qk, kk > 0 ? 1u : 0u);
+            umma_f16_ts_w(tmem + buf * 128u, tmem + S::q_col(qb) + 8u * kk, b_base + b_off, kHi, idesc_qk,
+                          kk > 0 ? 1u : 0u);
           }
         }
         umma_commit(&s_full[buf]);
+        umma_commit(&k_empty[slot]);
       }
     };
-    // O_h += P_h V_h over keys [64 h, 64 h + 64) for both halves: P_h from the first 32 columns of half h of
-    // S[buf], V rows from the stage of slot `slot`.
+    // O += P V over the tile's 128 keys: P of key half h from the first 32 columns of half h of S[buf], V rows
+    // from ring slot `slot`; frees the V slot.
     auto pv = [&](uint32_t buf, int slot, bool first) {
       if (lane == 0) {
-        const uint32_t b_base = v_lo + static_cast<uint32_t>((slot * S::kStageBytes) >> 4);
+        const uint32_t b_base = v_lo + static_cast<uint32_t>((slot * S::kTileBytes) >> 4);
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-#pragma unroll
-          for (int k4 = 0; k4 < 4; ++k4) {
-            const int kk = 4 * half + k4;  // 16-key step within the tile
-            umma_f16_ts_w(tmem + S::o_col(half), tmem + buf * 128u + 64u * half + 8u * k4,
-                          b_base + static_cast<uint32_t>((kk * 16 * 128) >> 4), kHi, idesc_pv,
-                          (!first || k4 > 0) ? 1u : 0u);
-          }
+        for (int kk = 0; kk < 8; ++kk) {  // 16-key steps
+          const uint32_t a_col = buf * 128u + 64u * (kk >> 2) + 8u * (kk & 3);
+          umma_f16_ts_w(tmem + S::kColO, tmem + a_col, b_base + static_cast<uint32_t>((kk * 16 * 128) >> 4), kHi,
+                        idesc_pv, (!first || kk > 0) ? 1u : 0u);
         }
         umma_commit(pv_done);
+        umma_commit(&v_empty[slot]);
       }
     };
     TileCursor cur, ahead;  // tile g and tile g + 2
     tile_cursor_init(a, cur);
     tile_cursor_init(a, ahead);
-    // prologue: S of the first two tiles
-    uint32_t g = 0;
-    for (int u = 0; u < 2 && ahead.valid; ++u) {
-      const int qb = (ahead.items_seen - 1) & 1;
-      if (ahead.j == 0) wait_lane0(&q_full[qb], ((ahead.items_seen - 1) >> 1) & 1, 75);
-      wait_lane0(&full[u], 0, 76 + u);
+    // QK of the tile `ahead` points at (index u) into S[u % 2]
+    auto issue_qk = [&](uint32_t u) {
+      const int qb = ahead.seg & 1;
+      if (ahead.j == 0) wait_lane0(&q_ready[qb], (ahead.seg >> 1) & 1, 75);
+      wait_lane0(&k_full[u % NS], (u / NS) & 1, 76);
       if (ok) {
         tc_fence_after_sync();
-        qk(u, qb, u);
-        if (lane == 0 && ahead.j + 1 == ahead.c.n) umma_commit(&q_empty[qb]);
+        qk(u & 1, qb, u % NS);
+        if (lane == 0 && ahead.j + 1 == ahead.c.n) umma_commit(&q_free[qb]);  // every QK of the segment issued
       }
       tile_cursor_advance(a, ahead);
-    }
+    };
+    for (uint32_t u = 0; u < 2 && ahead.valid; ++u) issue_qk(u);  // prologue: S of the first two tiles
+    uint32_t g = 0;
     while (cur.valid) {
       const uint32_t buf = g & 1;
-      const uint32_t u = g + 2;  // the stage holding V(g) and K(g + 2)
-      const int slot = u & 1;
       __syncwarp();
       named_barrier_sync(S::kBarP + buf, S::kBarPThreads);  // both halves of P(g) are in TMEM
-      wait_lane0(&full[slot], (u >> 1) & 1, 78);
+      wait_lane0(&v_full[g % NS], (g / NS) & 1, 77);
       if (ok) {
         tc_fence_after_sync();
-        pv(buf, slot, cur.j == 0);
-        if (lane == 0 && cur.j + 1 == cur.c.n) umma_commit(o_full);  // the item's O is complete
+        pv(buf, g % NS, cur.j == 0);
+        if (lane == 0 && cur.j + 1 == cur.c.n) umma_commit(o_full);  // the segment's O is complete
       }
-      if (ahead.valid) {
-        // S[buf] takes tile g + 2 (both halves of P(g) are consumed first, in issue order)
-        const int qb = (ahead.items_seen - 1) & 1;
-        if (ahead.j == 0) wait_lane0(&q_full[qb], ((ahead.items_seen - 1) >> 1) & 1, 79);
-        if (ok) {
-          tc_fence_after_sync();
-          qk(buf, qb, slot);
-          if (lane == 0 && ahead.j + 1 == ahead.c.n) umma_commit(&q_empty[qb]);  // every QK of that item issued
-        }
-        tile_cursor_advance(a, ahead);
-      }
+      if (ahead.valid) issue_qk(g + 2);  // S[buf] takes tile g + 2 (P(g) is consumed first, in issue order)
       tile_cursor_advance(a, cur);
       ++g;
     }
@@ -449,15 +425,21 @@ __global__ void __launch_bounds__(384, 1)
     __syncwarp();
   } else if (warp >= 4) {
     // ------------------------------------------------------------------------- softmax / epilogue
-    // Warpgroup 1 (warps 4-7) owns keys [0, 64) of every tile, warpgroup 2 (warps 8-11) keys [64, 128). A warp
-    // may only touch the TMEM lane quarter warp % 4, so each warpgroup covers all 128 rows.
+    // Warpgroup 1 (warps 4-7) owns keys [0, 64) of every tile and the first half of the columns of Q and O;
+    // warpgroup 2 (warps 8-11) keys [64, 128) and the second half. A warp may only touch the TMEM lane quarter
+    // warp % 4, so each warpgroup covers all 128 rows.
     setmaxnreg_inc<S::kRegsSoftmax>();
     const int half = (warp - 4) / 4;
     const int row = (warp % 4) * 32 + lane;  // TMEM lane = query row within the tile
     const uint32_t lane_base = static_cast<uint32_t>((warp % 4) * 32) << 16;
-    const uint32_t o_own = tmem + lane_base + S::o_col(half);
+    const int dh = D / 2;  // this warpgroup's elements of each Q row
+    // this warpgroup's columns of O: [o_lo, o_lo + o_n), split on a 16-column boundary (TMEM loads of 16 columns)
+    const int o_split = min(D, (D / 2 + 15) / 16 * 16);
+    const int o_lo = half ? o_split : 0;
+    const int o_n = half ? D - o_split : o_split;
+    const uint32_t o_own = tmem + lane_base + S::kColO + static_cast<uint32_t>(o_lo);
     bool ok = true;
-    uint32_t g = 0, items_done = 0;
+    uint32_t g = 0, segs_done = 0;
     auto wait_warp = [&](uint64_t* bar, uint32_t parity, int site) {
       if (ok) {
         ok = __all_sync(0xffffffffu, mbar_wait(bar, parity, a.budget_ns));
@@ -465,12 +447,42 @@ __global__ void __launch_bounds__(384, 1)
       }
       return ok;
     };
+    // Q of the next segment with tiles, into TMEM buffer (its index) % 2: this thread's row, this warpgroup's half
+    // of the head dimension, as packed 16-bit pairs (element 2c in the low half of column c), the layout of an A
+    // operand read from TMEM. Rows past the query length are zeros.
+    TileCursor qcur;
+    tile_cursor_init(a, qcur);
+    auto write_next_q = [&]() {
+      if (!qcur.valid) return;
+      const int qb = qcur.seg & 1;
+      if (qcur.seg >= 2) wait_warp(&q_free[qb], ((qcur.seg - 2) >> 1) & 1, 88);
+      const int qrow = qcur.c.q0 + row;
+      const uint4* src = reinterpret_cast<const uint4*>(
+          reinterpret_cast<const T*>(a.q) +
+          (((long long)qcur.c.b * a.sq + min(qrow, a.sq - 1)) * a.heads + qcur.c.h) * D + dh * half);
+      const uint32_t dst = tmem + lane_base + S::q_col(qb) + static_cast<uint32_t>(dh / 2 * half);
+      if (ok) {
+        for (int w = 0; w < dh / 8; ++w) {  // 8 elements (4 columns) per step
+          const uint4 v = qrow < a.sq ? src[w] : make_uint4(0, 0, 0, 0);
+          tmem_st4(dst + 4 * w, v.x, v.y, v.z, v.w);
+        }
+        tmem_wait_st();
+      }
+      tc_fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&q_ready[qb]);
+      // past the segment's tiles: the next segment with tiles
+      qcur.j = qcur.c.n - 1;
+      tile_cursor_advance(a, qcur);
+    };
+    write_next_q();  // segment 0
     SegmentWalk walk;
     segment_walk_init(a, walk);
     HalvesSegment sg;
     HalvesItem c;
     volatile int* merge_flag = reinterpret_cast<volatile int*>(smem + S::kTmemSlot + 4);
     while (segment_walk_next(a, walk, sg, c)) {
+      if (c.n > 0) write_next_q();  // the following segment's Q, while this one runs
       const int q = c.q0 + row;
       const bool row_valid = q < a.sq;
       const int vis = row_valid ? halves_visible(q, c.len, a.sq, a.causal) : 0;
@@ -504,6 +516,11 @@ __global__ void __launch_bounds__(384, 1)
           mx_raw = fmaxf(mx_raw, fmaxf(fmaxf(__uint_as_float(sr[col]), __uint_as_float(sr[col + 1])),
                                        fmaxf(__uint_as_float(sr[col + 2]), __uint_as_float(sr[col + 3]))));
         }
+        // the row's maximum over both key halves
+        xmax[((g & 1) * 2 + half) * 128 + row] = mx_raw;
+        __syncwarp();
+        named_barrier_sync(S::kBarX, 256);
+        mx_raw = fmaxf(mx_raw, xmax[((g & 1) * 2 + (half ^ 1)) * 128 + row]);
         const float mx = mx_raw * a.scale_log2;  // scale > 0; -inf stays -inf
         float m_new = m;
         bool grow = false;
@@ -512,6 +529,7 @@ __global__ void __launch_bounds__(384, 1)
         } else if (mx > m + 8.0f) {
           grow = true;
         }
+        // the same rows, maxima and running max in both warpgroups: both take the same decision
         const bool warp_grow = __any_sync(0xffffffffu, grow);
         float alpha = 1.f;
         if (warp_grow && j > 0) {
@@ -526,12 +544,13 @@ __global__ void __launch_bounds__(384, 1)
           halves_exp2_pack<Tr>(sr, make_float2(a.scale_log2, a.scale_log2), make_float2(neg_m, neg_m), acc, packed);
           tmem_st32(s_addr, packed);
         }
-        // O_h may be rescaled only once PV(g - 1) has completed (at most that PV is outstanding here).
+        // this warpgroup's columns of O may be rescaled only once PV(g - 1) has completed (at most that PV is
+        // outstanding here)
         if (warp_grow && j > 0) {
           wait_warp(pv_done, (g - 1) & 1, 82 + half);
           if (ok) {
             tc_fence_after_sync();
-            for (int cb = 0; cb < D / 16; ++cb) {
+            for (int cb = 0; cb < o_n / 16; ++cb) {
               uint32_t r[16];
               tmem_ld16(o_own + cb * 16, r);
               tmem_wait_ld();
@@ -541,14 +560,12 @@ __global__ void __launch_bounds__(384, 1)
             }
           }
         }
-        // Value rows past the cache end: this half's rows of V(g) are zeroed before its P is released (PV reads
-        // them). V(g) is in the stage u = g + 2.
+        // Value rows past the cache end: this half's rows of V(g) are zeroed before P is released (PV reads them)
         if (tok0 + BN > c.len) {
-          const uint32_t u = g + 2;
-          wait_warp(&full[u & 1], (u >> 1) & 1, 84 + half);
+          wait_warp(&v_full[g % NS], (g / NS) & 1, 84 + half);
           const int vrow = 64 * half + row;
           if (ok && row < 64 && tok0 + vrow >= c.len) {
-            uint8_t* dst = st_smem + (u & 1) * S::kStageBytes + vrow * 128;
+            uint8_t* dst = v_smem + (g % NS) * S::kTileBytes + vrow * 128;
 #pragma unroll
             for (int blk = 0; blk < NB; ++blk) {
 #pragma unroll
@@ -569,22 +586,16 @@ __global__ void __launch_bounds__(384, 1)
         m = m_new;
       }
       if (c.n > 0) {
-        wait_warp(o_full, items_done & 1, 86 + half);  // the item's last PV has completed
-        ++items_done;
+        wait_warp(o_full, segs_done & 1, 86 + half);  // the segment's last PV has completed
+        ++segs_done;
       }
-      // epilogue: merge the two halves' running states (LSE weights), then each warpgroup normalises and
-      // stores alternate 16-column blocks of the row
-      xch[(2 * half) * 128 + row] = m;
-      xch[(2 * half + 1) * 128 + row] = l;
+      // epilogue: the row sum over both halves, then each warpgroup normalises and stores its half of the row
+      xsum[half * 128 + row] = l;
       __syncwarp();  // the named barriers are the aligned form: the warp arrives converged
-      named_barrier_sync(S::kBarX, 256);  // both halves' states are published
-      const float m0 = xch[row], l0 = xch[128 + row], m1 = xch[256 + row], l1 = xch[384 + row];
-      const float mt = fmaxf(m0, m1);
-      const float w0 = (m0 == -INFINITY) ? 0.f : fast_exp2(m0 - mt);
-      const float w1 = (m1 == -INFINITY) ? 0.f : fast_exp2(m1 - mt);
-      const float lt = l0 * w0 + l1 * w1;
+      named_barrier_sync(S::kBarX, 256);
+      const float lt = l + xsum[(half ^ 1) * 128 + row];
       const float inv = lt > 0.f ? 1.f / lt : 0.f;
-      const float lse = (c.n > 0 && lt > 0.f) ? mt + fast_log2(lt) : kEmptyLse;
+      const float lse = (c.n > 0 && lt > 0.f) ? m + fast_log2(lt) : kEmptyLse;
       const long long row_id = row_valid ? ((long long)c.b * a.sq + q) * a.heads + c.h : 0;
       long long my_slot = 0;  // this program's slot for a piece (contiguous schedule)
       if (sg.piece) {
@@ -596,44 +607,33 @@ __global__ void __launch_bounds__(384, 1)
       }
       const bool read_o = c.n > 0 && ok;
       if (read_o) tc_fence_after_sync();
-      // this warpgroup's blocks cb = half, half + 2, ...: both O halves of up to four blocks loaded before one wait
-      constexpr int kBlocks = NB * 4;  // 16-column blocks of the O accumulators (D / 16 of them hold data)
+      for (int cb = 0; cb < o_n / 16; ++cb) {
+        float o[16];
+        if (read_o) {  // warp-collective: every lane, valid row or not
+          uint32_t r[16];
+          tmem_ld16(o_own + cb * 16, r);
+          tmem_wait_ld();
 #pragma unroll
-      for (int c0 = 0; c0 < kBlocks; c0 += 4) {
-        uint32_t r0[2][16], r1[2][16];
+          for (int i = 0; i < 16; ++i) o[i] = __uint_as_float(r[i]) * inv;
+        } else {
 #pragma unroll
-        for (int k = 0; k < 2; ++k) {
-          const int cb = c0 + 2 * k + half;
-          if (read_o && cb < D / 16) {  // warp-collective: every lane, valid row or not
-            tmem_ld16(tmem + lane_base + S::o_col(0) + cb * 16, r0[k]);
-            tmem_ld16(tmem + lane_base + S::o_col(1) + cb * 16, r1[k]);
-          }
+          for (int i = 0; i < 16; ++i) o[i] = 0.f;
         }
-        if (read_o) tmem_wait_ld();
+        const int col = o_lo + cb * 16;
+        if (row_valid && sg.piece) {
+          float4* dst = reinterpret_cast<float4*>(a.slot_o + (my_slot * 128 + row) * D + col);
 #pragma unroll
-        for (int k = 0; k < 2; ++k) {
-          const int cb = c0 + 2 * k + half;
-          if (cb >= D / 16) continue;
-          float o[16];
+          for (int i = 0; i < 4; ++i) dst[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+        } else if (row_valid && a.write_partials) {
+          float4* dst = reinterpret_cast<float4*>(a.part_o + (row_id * a.splits + c.s) * D + col);
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            o[i] = read_o ? (__uint_as_float(r0[k][i]) * w0 + __uint_as_float(r1[k][i]) * w1) * inv : 0.f;
-          }
-          if (row_valid && sg.piece) {
-            float4* dst = reinterpret_cast<float4*>(a.slot_o + (my_slot * 128 + row) * D + cb * 16);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) dst[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
-          } else if (row_valid && a.write_partials) {
-            float4* dst = reinterpret_cast<float4*>(a.part_o + (row_id * a.splits + c.s) * D + cb * 16);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) dst[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
-          } else if (row_valid) {
-            uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<T*>(a.out) + row_id * D + cb * 16);
-            dst[0] = make_uint4(Tr::pack2(o[0], o[1]), Tr::pack2(o[2], o[3]), Tr::pack2(o[4], o[5]),
-                                Tr::pack2(o[6], o[7]));
-            dst[1] = make_uint4(Tr::pack2(o[8], o[9]), Tr::pack2(o[10], o[11]), Tr::pack2(o[12], o[13]),
-                                Tr::pack2(o[14], o[15]));
-          }
+          for (int i = 0; i < 4; ++i) dst[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+        } else if (row_valid) {
+          uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<T*>(a.out) + row_id * D + col);
+          dst[0] = make_uint4(Tr::pack2(o[0], o[1]), Tr::pack2(o[2], o[3]), Tr::pack2(o[4], o[5]),
+                              Tr::pack2(o[6], o[7]));
+          dst[1] = make_uint4(Tr::pack2(o[8], o[9]), Tr::pack2(o[10], o[11]), Tr::pack2(o[12], o[13]),
+                              Tr::pack2(o[14], o[15]));
         }
       }
       if (row_valid && a.write_partials && half == 0) a.part_lse[row_id * a.splits + c.s] = lse;
@@ -644,13 +644,12 @@ __global__ void __launch_bounds__(384, 1)
         // finished last). No CTA waits for another.
         __threadfence();
         __syncwarp();
-        named_barrier_sync(S::kBarX, 256);  // both warpgroups have written their blocks
-        if (warp == 4 && lane == 0) {
-          const long long total = a.prog_u[a.programs];
-          const int q_first = program_of(total, a.programs, sg.item_u);
-          const int pieces = program_of(total, a.programs, sg.item_u + sg.units - 1) - q_first + 1;
-          *merge_flag = atomicAdd(&a.counters[sg.item], 1) + 1 == pieces ? 1 : 0;
-        }
+        named_barrier_sync(S::kBarX, 256);  // both warpgroups have written their halves
+        const long long total = a.prog_u[a.programs];
+        const int q_first = program_of(total, a.programs, sg.item_u);
+        const int pieces = program_of(total, a.programs, sg.item_u + sg.units - 1) - q_first + 1;
+        const int first_extra = sg.item_u != program_start(total, a.programs, q_first) ? 1 : 0;
+        if (warp == 4 && lane == 0) *merge_flag = atomicAdd(&a.counters[sg.item], 1) + 1 == pieces ? 1 : 0;
         __syncwarp();
         named_barrier_sync(S::kBarX, 256);
         const int merge = *merge_flag;
@@ -659,10 +658,6 @@ __global__ void __launch_bounds__(384, 1)
           if (warp == 4 && lane == 0) a.counters[sg.item] = 0;  // ready for the next launch
         }
         if (merge && row_valid) {
-          const long long total = a.prog_u[a.programs];
-          const int q_first = program_of(total, a.programs, sg.item_u);
-          const int pieces = program_of(total, a.programs, sg.item_u + sg.units - 1) - q_first + 1;
-          const int first_extra = sg.item_u != program_start(total, a.programs, q_first) ? 1 : 0;
           float peak = kEmptyLse;
           for (int k = 0; k < pieces; ++k) {
             peak = fmaxf(peak, __ldcg(&a.slot_lse[piece_slot(q_first, first_extra, k) * 128 + row]));
@@ -673,7 +668,8 @@ __global__ void __launch_bounds__(384, 1)
             if (lk > kValidLse) wsum += fast_exp2(lk - peak);
           }
           const float scale = wsum > 0.f ? 1.f / wsum : 0.f;
-          for (int cb = half; cb < D / 16; cb += 2) {
+          for (int cb = 0; cb < o_n / 16; ++cb) {
+            const int col = o_lo + cb * 16;
             float acc[16];
 #pragma unroll
             for (int i = 0; i < 16; ++i) acc[i] = 0.f;
@@ -682,7 +678,7 @@ __global__ void __launch_bounds__(384, 1)
               const float lk = __ldcg(&a.slot_lse[pr]);
               if (!(lk > kValidLse)) continue;
               const float w = fast_exp2(lk - peak);
-              const float4* src = reinterpret_cast<const float4*>(a.slot_o + pr * D + cb * 16);
+              const float4* src = reinterpret_cast<const float4*>(a.slot_o + pr * D + col);
 #pragma unroll
               for (int i = 0; i < 4; ++i) {
                 const float4 v = __ldcg(src + i);
@@ -692,7 +688,7 @@ __global__ void __launch_bounds__(384, 1)
                 acc[4 * i + 3] += w * v.w;
               }
             }
-            uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<T*>(a.out) + row_id * D + cb * 16);
+            uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<T*>(a.out) + row_id * D + col);
             dst[0] = make_uint4(Tr::pack2(acc[0] * scale, acc[1] * scale), Tr::pack2(acc[2] * scale, acc[3] * scale),
                                 Tr::pack2(acc[4] * scale, acc[5] * scale), Tr::pack2(acc[6] * scale, acc[7] * scale));
             dst[1] = make_uint4(Tr::pack2(acc[8] * scale, acc[9] * scale), Tr::pack2(acc[10] * scale, acc[11] * scale),
@@ -714,8 +710,8 @@ __global__ void __launch_bounds__(384, 1)
 }
 
 template <typename T, int NB>
-static cudaError_t launch_halves_t(const LaunchDesc& d, const HalvesArgs& args, const CUtensorMap& qmap,
-                                   const CUtensorMap& kmap, const CUtensorMap& vmap) {
+static cudaError_t launch_halves_t(const LaunchDesc& d, const HalvesArgs& args, const CUtensorMap& kmap,
+                                   const CUtensorMap& vmap) {
   using S = HalvesShape<NB>;
   auto kernel = fmha_halves_sm100_kernel<T, NB>;
   // setmaxnreg.inc only succeeds if the registers the block was launched with cover the new split (see
@@ -732,14 +728,15 @@ static cudaError_t launch_halves_t(const LaunchDesc& d, const HalvesArgs& args, 
   const long long grid = args.contiguous ? args.programs
                                          : std::min<long long>(args.items, std::min<long long>(cap, d.sm_count));
   if (grid <= 0) return cudaSuccess;
-  kernel<<<(unsigned)grid, S::kThreads, S::kBytes, d.stream>>>(qmap, kmap, vmap, args);
+  kernel<<<(unsigned)grid, S::kThreads, S::kBytes, d.stream>>>(kmap, vmap, args);
   return cudaGetLastError();
 }
 
-cudaError_t launch_tensor_halves(const LaunchDesc& d, bool write_partials, const CUtensorMap& qmap,
-                                 const CUtensorMap& kmap, const CUtensorMap& vmap, int box_rows) {
+cudaError_t launch_tensor_halves(const LaunchDesc& d, bool write_partials, const CUtensorMap& kmap,
+                                 const CUtensorMap& vmap, int box_rows) {
   const fgw_mha_params& p = d.p;
   HalvesArgs args;
+  args.q = p.q;
   args.out = p.out;
   args.table = p.block_table;
   args.lengths = d.lens;
@@ -772,12 +769,12 @@ cudaError_t launch_tensor_halves(const LaunchDesc& d, bool write_partials, const
   args.slot_o = d.slot_o;
   const bool bf16 = p.dtype == FGW_DTYPE_BFLOAT16;
   if (p.head_dim <= 64) {
-    return bf16 ? launch_halves_t<__nv_bfloat16, 1>(d, args, qmap, kmap, vmap)
-                : launch_halves_t<__half, 1>(d, args, qmap, kmap, vmap);
+    return bf16 ? launch_halves_t<__nv_bfloat16, 1>(d, args, kmap, vmap)
+                : launch_halves_t<__half, 1>(d, args, kmap, vmap);
   }
   if (p.head_dim <= 128) {
-    return bf16 ? launch_halves_t<__nv_bfloat16, 2>(d, args, qmap, kmap, vmap)
-                : launch_halves_t<__half, 2>(d, args, qmap, kmap, vmap);
+    return bf16 ? launch_halves_t<__nv_bfloat16, 2>(d, args, kmap, vmap)
+                : launch_halves_t<__half, 2>(d, args, kmap, vmap);
   }
   return cudaErrorInvalidValue;
 }

@@ -388,10 +388,10 @@ __global__ void __launch_bounds__(256, 1)
         uint32_t packed[BN / 2];
 #pragma unroll
         for (int i = 0; i < BN / 2; ++i) {
-          const float p0 = fast_exp2(s[2 * i] - m_use);
-          const float p1 = fast_exp2(s[2 * i + 1] - m_use);
-          rowsum += p0 + p1;
-          packed[i] = Tr::pack2(p0, p1);
+          packed[i] = Tr::pack2(fast_exp2(s[2 * i] - m_use), fast_exp2(s[2 * i + 1] - m_use));
+          // the row sum adds the rounded values PV multiplies (the lazily rescaled max lets P exceed 1 and round)
+          const float2 r = Tr::unpack2(packed[i]);
+          rowsum += r.x + r.y;
         }
         // PV of the previous tile must be finished before P is overwritten and O is rescaled.
         if (j > 0) wait_warp(pv_done, (pc - 1) & 1, 31);
@@ -574,7 +574,7 @@ cudaError_t launch_tensor(const LaunchDesc& d, bool write_partials) {
   }
   if (d.tensor_kernel == FGW_TENSOR_KERNEL_HALVES) {
     if (nb > 2) return cudaErrorNotSupported;
-    return launch_tensor_halves(d, write_partials, qmap, kmap, vmap, args.box_rows);
+    return launch_tensor_halves(d, write_partials, kmap, vmap, args.box_rows);  // Q goes to TMEM, not via TMA
   }
   if (d.tensor_kernel == FGW_TENSOR_KERNEL_PAIRS) {
     if (nb > 2) return cudaErrorNotSupported;

@@ -84,8 +84,8 @@ cudaError_t launch_tensor(const LaunchDesc& d, bool write_partials);
 cudaError_t launch_tensor_pairs(const LaunchDesc& d, bool write_partials, const CUtensorMap& qmap,
                                 const CUtensorMap& kmap, const CUtensorMap& vmap, int box_rows);
 // Key-halves tensor kernel (head_dim <= 128, opt-in); called by launch_tensor with its tensor maps.
-cudaError_t launch_tensor_halves(const LaunchDesc& d, bool write_partials, const CUtensorMap& qmap,
-                                 const CUtensorMap& kmap, const CUtensorMap& vmap, int box_rows);
+cudaError_t launch_tensor_halves(const LaunchDesc& d, bool write_partials, const CUtensorMap& kmap,
+                                 const CUtensorMap& vmap, int box_rows);
 
 // Which path AUTO picks, and which tcgen05 kernel the tensor path runs.
 int resolve_path(const fgw_mha_params& p);
