@@ -62,6 +62,8 @@ def parse_args(argv=None):
     p.add_argument("--splits", type=int, default=None, help="force num_splits for the headline workload")
     p.add_argument("--tensor-kernel", choices=["auto", "pairs", "single", "halves"], default="auto",
                    help="tcgen05 kernel of the long-query workloads")
+    p.add_argument("--task-assignment", choices=["strided", "contiguous", "tail"], default=None,
+                   help="schedule of the long-query workloads (default: the library's choice)")
     p.add_argument("--only", choices=["longq", "decode"], default=None, help="measure one workload (profiling)")
     p.add_argument("--decode-batch", type=int, default=DECODE["batch"],
                    help="requests in the decode workload (smaller values make profiling captures small)")
@@ -283,7 +285,8 @@ def run_longq(args, rank, world, device, stream):
     inp = longq_inputs(1000 + rank, device)
     kernel = build_kernel(c["batch"], c["sq"], c["heads"], c["dim"], inp["k"].shape[0], inp["width"], c["page"],
                           False, "bfloat16", device.index, num_splits=args.splits,
-                          full_kv_cache=True, path=args.path, tensor_kernel=args.tensor_kernel)
+                          full_kv_cache=True, path=args.path, tensor_kernel=args.tensor_kernel,
+                          task_assignment=args.task_assignment)
     ws = kernel.new_workspace(device)
     out = torch.empty_like(inp["q"])
     a = (inp["q"], inp["k"], inp["v"], inp["table"], inp["lengths"])
@@ -335,7 +338,7 @@ def run_longq(args, rank, world, device, stream):
     def forward(bufs, out_buf):
         return mha_paged_decode(bufs["q"], bufs["k"], bufs["v"], bufs["table"], bufs["lengths"], c["page"], False,
                                 num_splits=args.splits, path=args.path, cache_lengths=inp["host_lengths"], out=out_buf,
-                                tensor_kernel=args.tensor_kernel)
+                                tensor_kernel=args.tensor_kernel, task_assignment=args.task_assignment)
 
     def e2e_step():
         for key in host:

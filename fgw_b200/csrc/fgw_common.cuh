@@ -137,9 +137,15 @@ __device__ __forceinline__ bool mbar_wait_all(uint64_t* b0, uint32_t p0, uint64_
   }
 }
 
-// Named barrier over a subset of warps (id 0 is __syncthreads).
+// Named barrier over a subset of warps (id 0 is __syncthreads). These are the aligned forms: every lane of a
+// warp executes them together, so callers reconverge the warp (__syncwarp) first.
 __device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// Arrival on a named barrier without waiting (the waiting side calls named_barrier_sync with the same count).
+__device__ __forceinline__ void named_barrier_arrive(uint32_t id, uint32_t threads) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
 // ---------------------------------------------------------------------------------------

@@ -74,6 +74,11 @@ struct Fmha2Shape {
   static constexpr int kBytes = kTmemSlot + 16 + 1024;
 };
 
+// named barriers between the two softmax warpgroups (id 1 is the piece epilogue's): tile B waits on kBarTurnB for
+// tile A's exponentials of a KV tile, tile A on kBarTurnA for tile B's of the previous one
+constexpr uint32_t kBarTurnB = 2;
+constexpr uint32_t kBarTurnA = 3;
+
 struct PairItem {
   int b, h, s, q0, len, n_begin, n, n_tile[2];
 };
@@ -469,6 +474,14 @@ __global__ void __launch_bounds__(384, 1)
       const bool row_valid = q < a.sq;
       const int vis = row_valid ? visible_upto(q, c.len, a.sq, a.causal) : 0;
       const int n_t = t == 0 ? c.n_tile[0] : c.n_tile[1];
+      // The two tiles' softmaxes take turns on the exponentials: tile A's of KV tile j, then tile B's, then A's of
+      // j + 1, and so on. One warp's 128 exponentials of its rows keep its SM sub-partition's SFU busy about as
+      // long as the other tile's PV + QK keep the tensor core busy, so taking turns lets each tile's exponentials
+      // overlap the other tile's MMAs; running at once, the two would share the SFU, each take twice as long and
+      // fall into step, leaving the tensor core idle while both exponentiate. Items whose tiles see different
+      // numbers of KV tiles (causal, or a partial last pair) do not take turns. Both warpgroups derive `turns` and
+      // their barrier counts from the same item, so every arrival meets its wait.
+      const bool turns = c.n_tile[0] == c.n_tile[1] && c.n_tile[0] > 0;
       float m = -INFINITY, l = 0.f;
       for (int j = 0; j < n_t; ++j) {
         const int tok0 = (c.n_begin + j) * BN;
@@ -530,6 +543,10 @@ __global__ void __launch_bounds__(384, 1)
         const float neg_m = (m_new == -INFINITY) ? 0.f : -m_new;
         // P = 2^(s*scale - m): the packed 16-bit pairs overwrite the first 64 S columns (the whole row is
         // already in registers).
+        if (turns && (t == 1 || j > 0)) {
+          __syncwarp();
+          named_barrier_sync(t == 1 ? kBarTurnB : kBarTurnA, 256);  // the other tile's previous turn is over
+        }
         float rowsum = 0.f;
         if (ok) {
           const float2 scale2 = make_float2(a.scale_log2, a.scale_log2);
@@ -549,6 +566,10 @@ __global__ void __launch_bounds__(384, 1)
           }
           tmem_wait_st();
           rowsum = (acc[0].x + acc[0].y) + (acc[1].x + acc[1].y) + (acc[2].x + acc[2].y) + (acc[3].x + acc[3].y);
+        }
+        if (turns) {
+          __syncwarp();
+          named_barrier_arrive(t == 0 ? kBarTurnB : kBarTurnA, 256);  // the other tile's turn
         }
         // Value rows past the cache end: the first tile to use this V stage zeroes them before it
         // releases P (the PV reads them).
@@ -574,6 +595,10 @@ __global__ void __launch_bounds__(384, 1)
         if (lane == 0) mbar_arrive(&p_full[t]);
         l = l * alpha + rowsum;
         m = m_new;
+      }
+      if (turns && t == 0) {
+        __syncwarp();
+        named_barrier_sync(kBarTurnA, 256);  // tile B's last turn (every arrival is waited for)
       }
       if (c.n > 0) vbase += c.n;
       // epilogue

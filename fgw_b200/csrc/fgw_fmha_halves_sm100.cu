@@ -220,10 +220,6 @@ __device__ __forceinline__ void halves_exp2_pack(const uint32_t (&sr)[64], float
   }
 }
 
-__device__ __forceinline__ void named_barrier_arrive(uint32_t id, uint32_t threads) {
-  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(threads) : "memory");
-}
-
 template <typename T, int NB>
 __global__ void __launch_bounds__(384, 1)
     fmha_halves_sm100_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
