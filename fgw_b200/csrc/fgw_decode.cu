@@ -5,7 +5,7 @@
 //   * one persistent CTA per SM walks its share of the work items (request, query-row block, split, head),
 //     requests in descending-cache-length order (LPT): with one split the items' KV stages, laid end to end,
 //     are cut into one equal range per CTA (contiguous schedule; an item cut between CTAs is merged in place by
-//     the CTA completing it), otherwise whole items are dealt round-robin;
+//     the CTA completing it) when asked for, otherwise whole items are dealt in snake order (snake_item);
 //   * a producer warp streams each item's live KV pages into a shared-memory ring with TMA,
 //     one 3-D box {head_dim, 1, rows} per (page slice, K or V), driven by the block table;
 //   * eight consumer warps split a tile's tokens into groups of LPT lanes; each group owns
@@ -95,7 +95,7 @@ struct DecodeSegment {
 };
 
 struct DecodeCursor {
-  long long whole;  // next whole item (strided part)
+  long long round;  // next round of whole items (strided part, snake order)
   long long item;
   int off;
   long long u, u_end;
@@ -115,7 +115,7 @@ __device__ __forceinline__ int decode_units(const DecodeArgs& a, long long item)
 
 template <bool kContiguous>
 __device__ __forceinline__ void decode_cursor_init(const DecodeArgs& a, DecodeCursor& k) {
-  k.whole = blockIdx.x;
+  k.round = 0;
   k.item = kContiguous ? a.prog_item[blockIdx.x] : 0;
   k.off = kContiguous ? a.prog_off[blockIdx.x] : 0;
   k.u = kContiguous ? a.prog_u[blockIdx.x] : 0;
@@ -127,29 +127,18 @@ __device__ __forceinline__ void decode_cursor_init(const DecodeArgs& a, DecodeCu
 // the strided kernel carries none of the contiguous schedule's state (the consumers run at the register limit).
 template <int D, bool kContiguous>
 __device__ __forceinline__ bool decode_next(const DecodeArgs& a, DecodeCursor& k, DecodeSegment& sg) {
-  if (!kContiguous) {
-    if (k.whole >= a.items) return false;
-    sg.item = k.whole;
+  const long long whole = snake_item(k.round);
+  if (whole < (kContiguous ? static_cast<long long>(a.tail_start) : a.items)) {
+    sg.item = whole;
     sg.first = 0;
     sg.count = -1;
     sg.piece = false;
     sg.item_u = 0;
     sg.units = 0;
-    k.whole += gridDim.x;
+    ++k.round;
     return true;
   }
-  const long long whole_end = a.tail_start;
-  if (k.whole < whole_end) {
-    sg.item = k.whole;
-    sg.first = 0;
-    sg.count = -1;
-    sg.piece = false;
-    sg.item_u = 0;
-    sg.units = 0;
-    k.whole += gridDim.x;
-    return true;
-  }
-  if (k.u >= k.u_end) return false;
+  if (!kContiguous || k.u >= k.u_end) return false;
   const int units = decode_units<D>(a, k.item);
   const int count = static_cast<int>(min(static_cast<long long>(units - k.off), k.u_end - k.u));
   sg.item = k.item;

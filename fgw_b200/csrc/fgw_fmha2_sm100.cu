@@ -74,11 +74,6 @@ struct Fmha2Shape {
   static constexpr int kBytes = kTmemSlot + 16 + 1024;
 };
 
-// named barriers between the two softmax warpgroups (id 1 is the piece epilogue's): tile B waits on kBarTurnB for
-// tile A's exponentials of a KV tile, tile A on kBarTurnA for tile B's of the previous one
-constexpr uint32_t kBarTurnB = 2;
-constexpr uint32_t kBarTurnA = 3;
-
 struct PairItem {
   int b, h, s, q0, len, n_begin, n, n_tile[2];
 };
@@ -142,14 +137,14 @@ struct Segment {
 };
 
 struct SegmentCursor {
-  long long whole;  // next whole item (strided part)
+  long long round;  // next round of whole items (strided part, snake order)
   long long item;
   int off;
   long long u, u_end;
 };
 
 __device__ __forceinline__ void cursor_init(const Fmha2Args& a, SegmentCursor& k) {
-  k.whole = blockIdx.x;
+  k.round = 0;
   if (a.contiguous) {
     k.item = a.prog_item[blockIdx.x];
     k.off = a.prog_off[blockIdx.x];
@@ -166,13 +161,14 @@ __device__ __forceinline__ void cursor_init(const Fmha2Args& a, SegmentCursor& k
 // strided schedule, those of the full waves with the tail schedule), then its contiguous range of units.
 __device__ __forceinline__ bool next_segment(const Fmha2Args& a, SegmentCursor& k, Segment& sg) {
   const long long whole_end = a.contiguous ? a.tail_start : a.items;
-  if (k.whole < whole_end) {
-    sg.item = static_cast<int>(k.whole);
-    pair_item(a, k.whole, sg.c);
+  const long long whole = snake_item(k.round);
+  if (whole < whole_end) {
+    sg.item = static_cast<int>(whole);
+    pair_item(a, whole, sg.c);
     sg.piece = false;
     sg.item_u = sg.u0 = 0;
     sg.units = 0;
-    k.whole += gridDim.x;
+    ++k.round;
     return true;
   }
   if (!a.contiguous) return false;
@@ -474,14 +470,6 @@ __global__ void __launch_bounds__(384, 1)
       const bool row_valid = q < a.sq;
       const int vis = row_valid ? visible_upto(q, c.len, a.sq, a.causal) : 0;
       const int n_t = t == 0 ? c.n_tile[0] : c.n_tile[1];
-      // The two tiles' softmaxes take turns on the exponentials: tile A's of KV tile j, then tile B's, then A's of
-      // j + 1, and so on. One warp's 128 exponentials of its rows keep its SM sub-partition's SFU busy about as
-      // long as the other tile's PV + QK keep the tensor core busy, so taking turns lets each tile's exponentials
-      // overlap the other tile's MMAs; running at once, the two would share the SFU, each take twice as long and
-      // fall into step, leaving the tensor core idle while both exponentiate. Items whose tiles see different
-      // numbers of KV tiles (causal, or a partial last pair) do not take turns. Both warpgroups derive `turns` and
-      // their barrier counts from the same item, so every arrival meets its wait.
-      const bool turns = c.n_tile[0] == c.n_tile[1] && c.n_tile[0] > 0;
       float m = -INFINITY, l = 0.f;
       for (int j = 0; j < n_t; ++j) {
         const int tok0 = (c.n_begin + j) * BN;
@@ -543,10 +531,6 @@ __global__ void __launch_bounds__(384, 1)
         const float neg_m = (m_new == -INFINITY) ? 0.f : -m_new;
         // P = 2^(s*scale - m): the packed 16-bit pairs overwrite the first 64 S columns (the whole row is
         // already in registers).
-        if (turns && (t == 1 || j > 0)) {
-          __syncwarp();
-          named_barrier_sync(t == 1 ? kBarTurnB : kBarTurnA, 256);  // the other tile's previous turn is over
-        }
         float rowsum = 0.f;
         if (ok) {
           const float2 scale2 = make_float2(a.scale_log2, a.scale_log2);
@@ -566,10 +550,6 @@ __global__ void __launch_bounds__(384, 1)
           }
           tmem_wait_st();
           rowsum = (acc[0].x + acc[0].y) + (acc[1].x + acc[1].y) + (acc[2].x + acc[2].y) + (acc[3].x + acc[3].y);
-        }
-        if (turns) {
-          __syncwarp();
-          named_barrier_arrive(t == 0 ? kBarTurnB : kBarTurnA, 256);  // the other tile's turn
         }
         // Value rows past the cache end: the first tile to use this V stage zeroes them before it
         // releases P (the PV reads them).
@@ -595,10 +575,6 @@ __global__ void __launch_bounds__(384, 1)
         if (lane == 0) mbar_arrive(&p_full[t]);
         l = l * alpha + rowsum;
         m = m_new;
-      }
-      if (turns && t == 0) {
-        __syncwarp();
-        named_barrier_sync(kBarTurnA, 256);  // tile B's last turn (every arrival is waited for)
       }
       if (c.n > 0) vbase += c.n;
       // epilogue

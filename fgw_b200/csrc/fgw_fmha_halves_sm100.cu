@@ -120,14 +120,14 @@ struct HalvesSegment {
 };
 
 struct SegmentWalk {
-  long long whole;  // next whole item (strided part)
+  long long round;  // next round of whole items (strided part, snake order)
   long long item;
   int off;
   long long u, u_end;
 };
 
 __device__ __forceinline__ void segment_walk_init(const HalvesArgs& a, SegmentWalk& k) {
-  k.whole = blockIdx.x;
+  k.round = 0;
   k.item = a.contiguous ? a.prog_item[blockIdx.x] : 0;
   k.off = a.contiguous ? a.prog_off[blockIdx.x] : 0;
   k.u = a.contiguous ? a.prog_u[blockIdx.x] : 0;
@@ -140,13 +140,14 @@ __device__ __forceinline__ void segment_walk_init(const HalvesArgs& a, SegmentWa
 __device__ __forceinline__ bool segment_walk_next(const HalvesArgs& a, SegmentWalk& k, HalvesSegment& sg,
                                                   HalvesItem& c) {
   const long long whole_end = a.contiguous ? a.tail_start : a.items;
-  if (k.whole < whole_end) {
-    sg.item = k.whole;
+  const long long whole = snake_item(k.round);
+  if (whole < whole_end) {
+    sg.item = whole;
     sg.piece = false;
     sg.item_u = 0;
     sg.units = 0;
-    halves_item(a, k.whole, c);
-    k.whole += gridDim.x;
+    halves_item(a, whole, c);
+    ++k.round;
     return true;
   }
   if (!a.contiguous || k.u >= k.u_end) return false;
