@@ -55,11 +55,11 @@ long long stream_items(const fgw_mha_params& p) {
 // requests), so the CTAs read each token's row of all heads together and DRAM sees long runs; the contiguous cut
 // gives every CTA the same number of KV stages, but its CTAs walk different requests' 256-byte head slices, which
 // measured 0.75 of the HBM copy peak on config 5 against 0.99 strided.
-// Tensor path, key-halves kernel: the contiguous schedule (S double-buffering starts a segment's first QKs during
-// the previous segment, so cuts are cheap). Two-tile kernel: AUTO takes the contiguous schedule only when whole
-// items would leave more than a third of the programs idle in their single wave (items < 2/3 of the programs):
-// measured on config 2 (256 items, 148 programs, two waves) the strided schedule is faster there, since cutting
-// items adds segment starts and piece merges.
+// Tensor path, both tcgen05 kernels with contiguous forms (two-tile and key-halves): AUTO takes the contiguous
+// schedule only when whole items would leave more than a third of the programs idle in their single wave
+// (items < 2/3 of the programs). Measured on config 2 the strided schedule is faster: two-tile kernel (256
+// items, two waves) 120 us strided against 174 us contiguous, key-halves kernel (512 items) 158 against 214 us,
+// since cutting items adds segment starts and piece merges.
 bool use_stream_schedule(const fgw_mha_params& p) {
   if (p.schedule == FGW_SCHEDULE_STRIDED || p.num_splits != 1) return false;
   if (stream_items(p) > kStreamMaxItems) return false;
@@ -68,10 +68,9 @@ bool use_stream_schedule(const fgw_mha_params& p) {
   }
   if (p.head_dim > 128) return false;
   const int kernel = resolve_tensor_kernel(p);
-  if (kernel == FGW_TENSOR_KERNEL_HALVES) return true;
-  if (kernel != FGW_TENSOR_KERNEL_PAIRS) return false;
+  if (kernel != FGW_TENSOR_KERNEL_PAIRS && kernel != FGW_TENSOR_KERNEL_HALVES) return false;
   return p.schedule == FGW_SCHEDULE_CONTIGUOUS || p.schedule == FGW_SCHEDULE_TAIL ||
-         3 * pair_items(p) < 2ll * kStreamMaxPrograms;
+         3 * stream_items(p) < 2ll * kStreamMaxPrograms;
 }
 
 namespace {

@@ -9,8 +9,9 @@
 //     never waits for the tensor core;
 //   * Q lives in TMEM (two buffers: the next segment's Q is written while this one runs) and both products read
 //     their A operand from TMEM (tcgen05.mma with A in tensor memory): only K and V come from shared memory. A
-//     QK with Q in shared memory reads 8 KB of operands per M128 N128 K16 instruction, more than shared memory
-//     delivers in the instruction's 64 cycles (measured on B200: ~116 cycles each); with Q in TMEM it reads 4 KB;
+//     QK with Q in shared memory reads 8 KB of operands per M128 N128 K16 instruction, all that shared memory
+//     delivers (128 bytes per cycle) in the instruction's 64 cycles, leaving none for the row-max exchange; with
+//     Q in TMEM it reads 4 KB;
 //   * two softmax warpgroups: warps 4-7 own keys [0, 64) of every 128-key tile, warps 8-11 keys [64, 128). They
 //     exchange their partial row maxima through shared memory once per tile, so both halves exponentiate against
 //     the same running max and accumulate into one O; each keeps its own partial row sum;

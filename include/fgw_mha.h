@@ -79,9 +79,8 @@ typedef enum fgw_path {
  *               CONTIGUOUS over the items of the last, partial wave only (the reference's tail plan,
  *               static_schedule.py:83-116 `make_tail_plan`): only those items are cut into pieces.
  *   AUTO:       decode path: STRIDED (concurrent CTAs then read the heads of the same tokens together). Tensor
- *               path with one split: CONTIGUOUS for the HALVES kernel; for the PAIRS kernel CONTIGUOUS only when
- *               there are fewer work items than 2/3 of 148 programs (whole items would leave SMs idle), STRIDED
- *               otherwise.
+ *               path with one split, PAIRS and HALVES kernels: CONTIGUOUS only when there are fewer work items
+ *               than 2/3 of 148 programs (whole items would leave SMs idle), STRIDED otherwise.
  * CONTIGUOUS and TAIL apply with num_splits == 1 to the decode kernel and to the PAIRS and HALVES tensor kernels;
  * elsewhere the launch runs STRIDED (fgw_mha_resolve_schedule reports which).
  */

@@ -170,16 +170,21 @@ def test_resolved_schedule_per_path_and_kernel():
     assert _native.resolve_schedule(_params(schedule=_native.SCHEDULE_TAIL, **decode)) == _native.SCHEDULE_TAIL
     slots = 2 * 148 * 1 * (128 + 1) * 4  # D128 decode items carry one query row
     assert _native.workspace_size(_params(**contiguous)) >= _native.workspace_size(_params(**decode)) + slots
-    # tensor path: the two-tile and key-halves kernels take the contiguous cut (the key-halves kernel on AUTO, with
-    # 128-row slots); the one-tile kernel does not
+    # tensor path: the two-tile and key-halves kernels take the contiguous cut when asked for (with 256- and
+    # 128-row slots), and on AUTO only when whole items would leave a third of the programs idle; the one-tile
+    # kernel never does
     tensor = dict(q_len=4096, num_splits=1, path=_native.PATH_TENSOR, schedule=_native.SCHEDULE_CONTIGUOUS)
     assert _native.resolve_schedule(_params(**tensor)) == _native.SCHEDULE_CONTIGUOUS
-    halves = dict(tensor, schedule=_native.SCHEDULE_AUTO, tensor_kernel=_native.TENSOR_KERNEL_HALVES, batch=8,
-                  heads=16)
+    halves = dict(tensor, tensor_kernel=_native.TENSOR_KERNEL_HALVES, batch=8, heads=16)
     assert _native.resolve_schedule(_params(**halves)) == _native.SCHEDULE_CONTIGUOUS
     assert (_native.workspace_size(_params(**halves))
             >= _native.workspace_size(_params(**dict(halves, schedule=_native.SCHEDULE_STRIDED)))
             + 2 * 148 * 128 * (128 + 1) * 4)
+    for kernel in (_native.TENSOR_KERNEL_PAIRS, _native.TENSOR_KERNEL_HALVES):
+        auto = dict(tensor, schedule=_native.SCHEDULE_AUTO, tensor_kernel=kernel, batch=2, heads=8)  # config 2
+        assert _native.resolve_schedule(_params(**auto)) == _native.SCHEDULE_STRIDED
+        few = dict(auto, q_len=512, heads=4)  # 8 or 16 items: one partial wave
+        assert _native.resolve_schedule(_params(**few)) == _native.SCHEDULE_CONTIGUOUS
     assert _native.resolve_schedule(_params(tensor_kernel=_native.TENSOR_KERNEL_SINGLE, **tensor)) == \
         _native.SCHEDULE_STRIDED
     with pytest.raises(_native.FgwError):
