@@ -492,7 +492,7 @@ def run_decode_serving(args, dc, rank, world, device, stream):
     from fgw_b200.operators.mha.sharded import mha_paged_decode_sharded
     inp = dc["inp"]
     steps = max(10, args.steps)
-    base = np.asarray(inp["host_lengths"], dtype=np.int64)
+    base = np.asarray(inp["host_lengths"], dtype=np.int32)  # the cache_seqlens dtype, kept on the host as well
     host_q = inp["q"].cpu().pin_memory()
     host_len = torch.empty(base.shape[0], dtype=torch.int32).pin_memory()
     host_out = torch.empty(inp["q"].shape, dtype=inp["q"].dtype).pin_memory()

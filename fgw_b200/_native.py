@@ -7,6 +7,8 @@ There is no fallback: if the library is missing or cannot be loaded, every entry
 import ctypes
 import pathlib
 
+import numpy as np
+
 LIB_PATH = pathlib.Path(__file__).resolve().parent / "_lib" / "libfgw_mha.so"
 
 # fgw_status codes
@@ -38,12 +40,13 @@ TENSOR_KERNEL_PAIRS = 1
 TENSOR_KERNEL_SINGLE = 2
 TENSOR_KERNEL_HALVES = 3
 
-ABI_VERSION = 4  # FGW_MHA_ABI_VERSION the Params / GatherParams layouts below match
+ABI_VERSION = 5  # FGW_MHA_ABI_VERSION the Params / GatherParams / SplitModel layouts below match
 
 EXPORTED = (
     "fgw_mha_abi_version",
     "fgw_mha_status_string",
     "fgw_mha_device_sm_count",
+    "fgw_mha_choose_splits",
     "fgw_mha_resolve_path",
     "fgw_mha_resolve_schedule",
     "fgw_mha_workspace_size",
@@ -103,6 +106,45 @@ class Params(ctypes.Structure):
     ]
 
 
+SPLIT_MODEL_FEATURES = 10  # FGW_SPLIT_MODEL_FEATURES
+
+
+class SplitModel(ctypes.Structure):
+    """Mirror of ``fgw_split_model`` (include/fgw_mha.h): the B200 split cost model's weights and selection rule."""
+
+    _fields_ = [
+        ("weights", ctypes.c_double * SPLIT_MODEL_FEATURES),
+        ("floor_single_us", ctypes.c_double),
+        ("floor_multi_us", ctypes.c_double),
+        ("tolerance", ctypes.c_double),
+        ("absolute_margin_us", ctypes.c_double),
+    ]
+
+    @classmethod
+    def from_model(cls, model):
+        """From the version-3 model dict (models/b200_general_split_cost_model.json)."""
+        if model["version"] != 3 or len(model["weights"]) != SPLIT_MODEL_FEATURES:
+            raise ValueError("the native split choice takes the version-3 model")
+        m = cls()
+        m.weights[:] = [float(w) for w in model["weights"]]
+        m.floor_single_us = model["latency_floor_us"]["single"]
+        m.floor_multi_us = model["latency_floor_us"]["multi"]
+        m.tolerance = model["selection_tolerance"]
+        m.absolute_margin_us = model.get("absolute_selection_margin_us", 0.0)
+        return m
+
+
+class SplitChoice(ctypes.Structure):
+    """Mirror of ``fgw_split_choice``."""
+
+    _fields_ = [
+        ("splits", ctypes.c_int32),
+        ("full_kv_cache", ctypes.c_int32),
+        ("min_length", ctypes.c_int32),
+        ("max_length", ctypes.c_int32),
+    ]
+
+
 class GatherParams(ctypes.Structure):
     """Mirror of ``fgw_gather_params`` (include/fgw_mha.h)."""
 
@@ -156,6 +198,9 @@ def library():
     lib.fgw_mha_status_string.restype = ctypes.c_char_p
     lib.fgw_mha_device_sm_count.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_int)]
     lib.fgw_mha_device_sm_count.restype = ctypes.c_int
+    # fgw_mha_choose_splits runs on every serving call: no argtypes (their per-argument conversion costs more than
+    # the call), so choose_splits passes ctypes pointers and Python ints (C int by default)
+    lib.fgw_mha_choose_splits.restype = ctypes.c_int
     lib.fgw_mha_resolve_path.argtypes = [p, ctypes.POINTER(ctypes.c_int)]
     lib.fgw_mha_resolve_path.restype = ctypes.c_int
     lib.fgw_mha_resolve_schedule.argtypes = [p, ctypes.POINTER(ctypes.c_int)]
@@ -200,6 +245,21 @@ def device_sm_count(device):
     out = ctypes.c_int(0)
     check(library().fgw_mha_device_sm_count(int(device), ctypes.byref(out)), "fgw_mha_device_sm_count")
     return out.value
+
+
+_INT32 = np.dtype(np.int32)
+
+
+def choose_splits(model, host_lengths, batch, q_len, heads, head_dim, page_size, table_width, sm_count):
+    """``fgw_mha_choose_splits`` on a C-contiguous int32 NumPy array of host cache lengths: returns the filled
+    ``SplitChoice`` and the status (FGW_ERR_INVALID_ARGUMENT when a length is outside the table capacity)."""
+    if host_lengths.dtype is not _INT32 or host_lengths.shape != (batch,) or host_lengths.strides != (4,):
+        raise ValueError("host_lengths must be a C-contiguous int32 array of the batch's lengths")
+    choice = SplitChoice()
+    status = library().fgw_mha_choose_splits(
+        ctypes.byref(model), ctypes.c_void_p(host_lengths.__array_interface__["data"][0]), int(batch), int(q_len),
+        int(heads), int(head_dim), int(page_size), int(table_width), int(sm_count), ctypes.byref(choice))
+    return choice, status
 
 
 def resolve_path(params):

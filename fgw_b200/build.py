@@ -24,8 +24,10 @@ LIB_DIR = PACKAGE / "_lib"
 LIB = LIB_DIR / "libfgw_mha.so"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+# Host code keeps separate multiplies and adds (no fused multiply-add contraction): the host split choice
+# (fgw_split_choice.cu) must round like its Python restatement to make the same picks.
 CFLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
-          "--expt-relaxed-constexpr", "-DNDEBUG", f"-I{INCLUDE}", f"-I{CSRC}"]
+          "--expt-relaxed-constexpr", "-DNDEBUG", "-Xcompiler", "-ffp-contract=off", f"-I{INCLUDE}", f"-I{CSRC}"]
 
 
 def nvcc():

@@ -8,6 +8,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <vector>
 
 #include "fgw_common.cuh"
 #include "fgw_kernels.h"
@@ -212,6 +213,35 @@ static int device_sm_count_cached(int device, int* sms) {
   return FGW_OK;
 }
 
+cudaError_t prepare_kernel(const void* kernel, int smem_bytes, int device, int* regs) {
+  struct Prepared {
+    const void* kernel;
+    int device, smem_bytes, regs;
+  };
+  static std::mutex mu;
+  static std::vector<Prepared> done;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    for (const Prepared& k : done) {
+      if (k.kernel == kernel && k.device == device && k.smem_bytes >= smem_bytes) {
+        if (regs != nullptr) *regs = k.regs;
+        return cudaSuccess;
+      }
+    }
+  }
+  cudaFuncAttributes attr;
+  cudaError_t err = cudaFuncGetAttributes(&attr, kernel);
+  if (err != cudaSuccess) return err;
+  if (smem_bytes > 0) {
+    err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+    if (err != cudaSuccess) return err;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  done.push_back({kernel, device, smem_bytes, attr.numRegs});
+  if (regs != nullptr) *regs = attr.numRegs;
+  return cudaSuccess;
+}
+
 static int prepare(const fgw_mha_params* params, void* workspace, size_t workspace_bytes_given, void* stream,
                    LaunchDesc& d) {
   int st = validate(params);
@@ -223,6 +253,7 @@ static int prepare(const fgw_mha_params* params, void* workspace, size_t workspa
   if (workspace_bytes_given < workspace_bytes(d.p, path)) return FGW_ERR_WORKSPACE_TOO_SMALL;
   int device = 0;
   if (cudaGetDevice(&device) != cudaSuccess) return FGW_ERR_NO_DEVICE;
+  d.device = device;
   st = device_sm_count_cached(device, &d.sm_count);
   if (st != FGW_OK) return st;
   if (encode_tiled() == nullptr) return FGW_ERR_CUDA;

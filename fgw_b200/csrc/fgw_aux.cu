@@ -173,7 +173,7 @@ cudaError_t launch_plan(const LaunchDesc& d) {
   while (n < batch) n <<= 1;
   const size_t smem = batch <= kPlanSortMax ? n * sizeof(unsigned long long) : 0;
   if (smem > 32 * 1024) {
-    cudaError_t err = cudaFuncSetAttribute(plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t err = prepare_kernel(reinterpret_cast<const void*>(plan_kernel), (int)smem, d.device, nullptr);
     if (err != cudaSuccess) return err;
   }
   StreamPlanArgs sp{};

@@ -597,7 +597,7 @@ static cudaError_t launch_decode_t(const LaunchDesc& d, const DecodeArgs& args, 
   using S = DecodeShape<D>;
   using M = DecodeSmem<T, D>;
   auto kernel = args.contiguous ? decode_kernel<T, D, true> : decode_kernel<T, D, false>;
-  cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, M::kBytes);
+  cudaError_t err = prepare_kernel(reinterpret_cast<const void*>(kernel), M::kBytes, d.device, nullptr);
   if (err != cudaSuccess) return err;
   long long grid = args.items;
   const long long cap = d.p.grid_cap > 0 ? d.p.grid_cap : d.sm_count;

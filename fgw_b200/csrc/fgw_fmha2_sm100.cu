@@ -714,13 +714,11 @@ static cudaError_t launch_fmha2_t(const LaunchDesc& d, const Fmha2Args& args, co
   // setmaxnreg.inc only succeeds if the registers the block was launched with cover the new split:
   // warpgroup 0 drops to kRegsControl per thread, the two softmax warpgroups rise to kRegsSoftmax. Refuse
   // to launch a build whose allocation would not cover that (the increase would otherwise never complete).
-  cudaFuncAttributes attr;
-  cudaError_t err = cudaFuncGetAttributes(&attr, kernel);
+  int regs = 0;
+  cudaError_t err = prepare_kernel(reinterpret_cast<const void*>(kernel), S::kBytes, d.device, &regs);
   if (err != cudaSuccess) return err;
-  const int allocated = ((attr.numRegs + 7) / 8) * 8 * S::kThreads;
+  const int allocated = ((regs + 7) / 8) * 8 * S::kThreads;
   if (allocated < 4 * 32 * S::kRegsControl + 8 * 32 * S::kRegsSoftmax) return cudaErrorNotSupported;
-  err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kBytes);
-  if (err != cudaSuccess) return err;
   const long long cap = d.p.grid_cap > 0 ? d.p.grid_cap : d.sm_count;
   // contiguous schedule: one CTA per program of the plan; strided: persistent CTAs over the items
   const long long grid = args.contiguous ? args.programs

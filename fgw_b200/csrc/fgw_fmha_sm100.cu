@@ -532,7 +532,7 @@ static cudaError_t launch_tensor_t(const LaunchDesc& d, const TensorArgs& args, 
                                    const CUtensorMap& kmap, const CUtensorMap& vmap) {
   using L = TensorSmem<NB>;
   auto kernel = fmha_sm100_kernel<T, NB>;
-  cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
+  cudaError_t err = prepare_kernel(reinterpret_cast<const void*>(kernel), L::kBytes, d.device, nullptr);
   if (err != cudaSuccess) return err;
   const long long cap = d.p.grid_cap > 0 ? d.p.grid_cap : d.sm_count;
   const long long grid = std::min<long long>(args.items, std::min<long long>(cap, d.sm_count));

@@ -21,6 +21,7 @@ constexpr int kPairRows = 256;
 // Resolved launch description shared by every kernel family.
 struct LaunchDesc {
   fgw_mha_params p;
+  int device;         // the current CUDA device of the call
   // workspace carve-up (device pointers)
   WorkspaceHeader* header;
   int32_t* lens;      // [batch] cache lengths clamped into [0, table_width * page_size]
@@ -55,6 +56,11 @@ struct LaunchDesc {
 long long pair_items(const fgw_mha_params& p);
 // Query rows of one decode work item, and tokens of one decode pipeline stage (fgw_decode.cu).
 int decode_rows_per_item(int head_dim);
+
+// Once per kernel, device and shared-memory size instead of on every call: opts the kernel into
+// `smem_bytes` of dynamic shared memory (an attribute of the function in the device's context) and reports the
+// registers per thread the build gave it (`regs` may be null).
+cudaError_t prepare_kernel(const void* kernel, int smem_bytes, int device, int* regs);
 int decode_tile_tokens(int head_dim);
 // Work items the contiguous schedule lays end to end: the two-tile kernel's on the tensor path, the decode
 // kernel's (request, query-row block, head) on the decode path.

@@ -86,6 +86,37 @@ def _b200_model():
     return general_model.load_model(3)  # the B200 feature set fitted on B200 split sweeps
 
 
+@functools.lru_cache(maxsize=1)
+def _native_split_model():
+    """The B200 model as the library's ``fgw_split_model`` (built once)."""
+    return _native.SplitModel.from_model(_b200_model())
+
+
+_route_cached = functools.lru_cache(maxsize=64)(route)
+
+
+def _current_stream(device):
+    """Raw handle of the current CUDA stream of device index ``device``."""
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+if hasattr(torch._C, "_cuda_getCurrentRawStream"):
+    def _current_stream(device):  # noqa: F811 -- the same handle without building a Stream object
+        return torch._C._cuda_getCurrentRawStream(device)
+
+
+def _host_lengths(lengths, batch, capacity):
+    """Host cache lengths as a C-contiguous int32 array; values that int32 cannot hold are out of range."""
+    host = np.asarray(lengths)
+    if host.shape != (batch,):
+        raise ValueError("metadata shape mismatch")
+    if host.dtype != np.int32:
+        if host.size and (int(host.min()) < 0 or int(host.max()) > capacity):
+            raise ValueError("Cache lengths must be within table capacity")
+        host = host.astype(np.int32)
+    return np.ascontiguousarray(host)
+
+
 def _select_auto_splits(batch, sq, heads, dim, width, page_size, lengths, cores, chosen=None):
     """B200 split choice from host-known lengths (or table capacity) with the fitted B200 model; ``chosen`` is
     that choice when the caller has already made it."""
@@ -258,8 +289,7 @@ def build_kernel(batch, sq, heads, dim, pool_rows, width, page_size, causal, dty
     def launch(q, k, v, table, lengths, out=None, workspace=None):
         out = torch.empty_like(q) if out is None else out
         ws = _workspace(q.device) if workspace is None else workspace
-        stream = torch.cuda.current_stream(q.device).cuda_stream
-        _native.paged_fwd(_bind(q, k, v, table, lengths, out), ws.data_ptr(), ws.numel(), stream)
+        _native.paged_fwd(_bind(q, k, v, table, lengths, out), ws.data_ptr(), ws.numel(), _current_stream(q.get_device()))
         return out
 
     def plan_kernel(q, k, v, table, lengths, workspace):
@@ -336,8 +366,10 @@ def _check_inputs(q, k_cache, v_cache, block_table, cache_seqlens):
         raise ValueError("matching FP16/BF16 Q/K/V required")
     if block_table.dtype != torch.int32 or cache_seqlens.dtype != torch.int32:
         raise ValueError("int32 metadata required")
-    inputs = (q, k_cache, v_cache, block_table, cache_seqlens)
-    if q.device.type != "cuda" or any(x.device != q.device or not x.is_contiguous() for x in inputs):
+    dev = q.get_device() if q.is_cuda else -1
+    if (dev < 0 or k_cache.get_device() != dev or v_cache.get_device() != dev or block_table.get_device() != dev
+            or cache_seqlens.get_device() != dev or not q.is_contiguous() or not k_cache.is_contiguous()
+            or not v_cache.is_contiguous() or not block_table.is_contiguous() or not cache_seqlens.is_contiguous()):
         raise ValueError("contiguous inputs on the same CUDA device required")
     return b, sq, h, d
 
@@ -356,23 +388,21 @@ def mha_paged_decode(q, k_cache, v_cache, block_table, cache_seqlens, page_size,
     b, sq, h, d = _check_inputs(q, k_cache, v_cache, block_table, cache_seqlens)
     width = block_table.shape[1]
     capacity = width * page_size
-    route(q.dtype, d, page_size, sq, is_causal, cube_mode)  # the reference's route checks (ValueError)
-    lengths = np.asarray(cache_lengths if cache_lengths is not None else cache_seqlens.cpu().numpy())
-    if lengths.shape != (b,):
-        raise ValueError("metadata shape mismatch")
-    if b and (int(lengths.min()) < 0 or int(lengths.max()) > capacity):
+    _route_cached(q.dtype, d, page_size, sq, bool(is_causal), cube_mode)  # the reference's route checks
+    host = _host_lengths(cache_lengths if cache_lengths is not None else cache_seqlens.cpu().numpy(), b, capacity)
+    # One pass over the host lengths in the library: their range check, whether every cache is full, and the
+    # B200 model's split choice (it reads the lengths only through their KV-tile sum and maximum), so the
+    # launcher below is cached per shape and split count and a new length list costs no rebuild.
+    device = q.get_device()
+    choice, status = _native.choose_splits(_native_split_model(), host, b, sq, h, d, page_size, width,
+                                           sm_count(device))
+    if status != _native.OK:
         raise ValueError("Cache lengths must be within table capacity")
-    full_kv_cache = bool(int(lengths.min()) == capacity)
+    full_kv_cache = bool(choice.full_kv_cache)
     dtype_name = "float16" if q.dtype == torch.float16 else "bfloat16"
-    # The B200 model reads the lengths only through their KV-tile sum and maximum: the choice is made here,
-    # so the launcher below is cached per shape and split count and a new length list costs no rebuild.
-    auto = None
-    if num_splits is None and split_policy != "legacy":
-        stats = general_model.tile_stats(lengths.tolist() if b <= 64 else lengths)
-        auto = general_model.select_b200_splits(b, sq, h, d, page_size, width, *stats, model=_b200_model(),
-                                                cores=sm_count(q.device.index))
+    auto = choice.splits if num_splits is None and split_policy != "legacy" else None
     kernel = build_kernel(b, sq, h, d, k_cache.shape[0], width, page_size, bool(is_causal), dtype_name,
-                          q.device.index, pipeline_stages=pipeline_stages, buffer_versions=buffer_versions,
+                          device, pipeline_stages=pipeline_stages, buffer_versions=buffer_versions,
                           q_resident=q_resident, kv_versions=kv_versions, schedule_mode=schedule_mode,
                           num_splits=num_splits, split_policy=split_policy, full_kv_cache=full_kv_cache,
                           persistent_programs=persistent_programs, cube_mode=cube_mode, cache_lengths=None,

@@ -22,6 +22,9 @@
  *                           (v7_experimental.py:842-855: direct_kernel / partial_kernel / merge_kernel).
  *   fgw_mha_device_sm_count the core count the reference reads from the device properties
  *                           (v7.py:65-68, 104-107 `cube_core_num`).
+ *   fgw_mha_choose_splits   the host-side split choice from the cache lengths before each launch:
+ *                           operators/mha/general_split_cost_model.py:70-91 (`predict_us`,
+ *                           `select_model_splits`), with the B200 model's features and weights.
  *   fgw_paged_cache_gather  the paged-cache gather pre-pass FGW pins from TileOPs and runs before attention
  *                           in its gather experiment: third_party/tileops_yyttt6/paged_cache_gather.py:108-232
  *                           (`_compile`), :44-104 (`_compile_generic`), :264-296 (`forward`); call site
@@ -37,7 +40,7 @@
 extern "C" {
 #endif
 
-#define FGW_MHA_ABI_VERSION 4
+#define FGW_MHA_ABI_VERSION 5
 
 #if defined(__GNUC__)
 #define FGW_API __attribute__((visibility("default")))
@@ -142,6 +145,28 @@ typedef struct fgw_mha_params {
   int32_t reserved[2];    /* must be zero */
 } fgw_mha_params;
 
+/* The B200 split cost model (version 3): latency prediction = sum of weights[i] x feature i over the ten
+ * features (constant, decode serial tiles, tensor serial tiles, decode waves, tensor waves, has merge, splits,
+ * merge rows x splits, longest partition excess, contiguous pieces per item), floored at floor_single_us (one
+ * split) or floor_multi_us; the choice is the smallest candidate (1, 2, ..., 128, at most the table's 128-token
+ * tiles) whose prediction is within max(tolerance x best, absolute_margin_us) of the best. The values ship in
+ * fgw_b200/operators/mha/models/b200_general_split_cost_model.json. */
+#define FGW_SPLIT_MODEL_FEATURES 10
+typedef struct fgw_split_model {
+  double weights[FGW_SPLIT_MODEL_FEATURES];
+  double floor_single_us;
+  double floor_multi_us;
+  double tolerance;
+  double absolute_margin_us;
+} fgw_split_model;
+
+typedef struct fgw_split_choice {
+  int32_t splits;         /* the model's split count (0 when the lengths are out of range) */
+  int32_t full_kv_cache;  /* 1 when every cache length equals the table capacity */
+  int32_t min_length;
+  int32_t max_length;
+} fgw_split_choice;
+
 /* ABI version of the loaded library (FGW_MHA_ABI_VERSION it was built with). */
 FGW_API int fgw_mha_abi_version(void);
 
@@ -150,6 +175,14 @@ FGW_API const char* fgw_mha_status_string(int status);
 
 /* Streaming multiprocessors of a CUDA device (148 on B200). */
 FGW_API int fgw_mha_device_sm_count(int device, int* sm_count);
+
+/* Host-only (no device work, no CUDA call): checks the host copy of the cache lengths against the table capacity
+ * (page_size x table_width) and chooses the split count with the B200 model, in one pass over the lengths.
+ * Returns FGW_ERR_INVALID_ARGUMENT for lengths outside [0, capacity] (choice->min_length / max_length still
+ * report them) or non-positive extents. */
+FGW_API int fgw_mha_choose_splits(const fgw_split_model* model, const int32_t* host_lengths, int batch, int q_len,
+                                  int heads, int head_dim, int page_size, int table_width, int sm_count,
+                                  fgw_split_choice* choice);
 
 /* Kernel path AUTO resolves to for these parameters (FGW_PATH_DECODE or FGW_PATH_TENSOR). */
 FGW_API int fgw_mha_resolve_path(const fgw_mha_params* params, int* path);

@@ -26,7 +26,7 @@ def test_library_loads_and_exports_every_declared_symbol():
     lib = _native.library()
     for name in declared_functions():
         assert hasattr(lib, name), name
-    assert _native.abi_version() == _native.ABI_VERSION == 4
+    assert _native.abi_version() == _native.ABI_VERSION == 5
 
 
 def test_status_strings():
