@@ -51,11 +51,11 @@ long long stream_items(const fgw_mha_params& p) {
   return static_cast<long long>(p.batch) * ((p.q_len + rows - 1) / rows) * p.heads * p.num_splits;
 }
 
-// Decode path, one split: CONTIGUOUS or TAIL when asked for; AUTO deals whole items strided. Dealt round-robin in
-// longest-first order with heads innermost, ~148 consecutive items are in flight at once (the heads of a few
-// requests), so the CTAs read each token's row of all heads together and DRAM sees long runs; the contiguous cut
-// gives every CTA the same number of KV stages, but its CTAs walk different requests' 256-byte head slices, which
-// measured 0.75 of the HBM copy peak on config 5 against 0.99 strided.
+// Decode path, one split: CONTIGUOUS or TAIL when asked for; AUTO deals whole items dynamically (a counter hands
+// the next item, longest request first with heads innermost, to whichever CTA asks), so the items in flight at
+// once are consecutive ones (the heads of a few requests) and DRAM sees long runs of each token's rows; the
+// contiguous cut gives every CTA the same number of KV stages, but its CTAs walk different requests' 256-byte
+// head slices, which measured 0.75 of the HBM copy peak on config 5 against 0.99-1.03 for whole items.
 // Tensor path, both tcgen05 kernels with contiguous forms (two-tile and key-halves): AUTO takes the contiguous
 // schedule only when whole items would leave more than a third of the programs idle in their single wave
 // (items < 2/3 of the programs). Measured on config 2 the strided schedule is faster: two-tile kernel (256

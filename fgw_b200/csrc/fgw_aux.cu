@@ -73,6 +73,8 @@ __global__ void __launch_bounds__(1024) plan_kernel(const int32_t* __restrict__ 
   if (threadIdx.x == 0) {
     ws->error = 0;
     ws->error_site = 0;
+    ws->finished = 0;
+    ws->next_item = 0;
   }
   // the decode kernel's fused split merge counts arrivals per row group from zero
   for (int i = threadIdx.x; i < merge_groups; i += blockDim.x) merge_counters[i] = 0;

@@ -27,8 +27,10 @@ constexpr float kValidLse = -1.0e29f;
 struct WorkspaceHeader {
   int32_t error;        // first fgw_status recorded by a device thread, 0 when clean
   int32_t error_site;   // which wait gave up (kernel-defined id)
-  uint32_t counter;     // reserved
-  uint32_t pad[61];
+  uint32_t finished;    // decode kernel's dynamic deal: CTAs that have drawn their last item
+  uint32_t pad0;
+  unsigned long long next_item;  // decode kernel's dynamic deal: next whole item to hand out
+  uint32_t pad[58];
 };
 static_assert(sizeof(WorkspaceHeader) == 256, "workspace header is 256 bytes");
 

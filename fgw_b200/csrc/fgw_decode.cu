@@ -71,7 +71,9 @@ struct DecodeSmem {
   static constexpr int kStageBytes = 2 * S::kTile * D * (int)sizeof(T);
   static constexpr int kStages = std::min(8, std::max(2, (192 * 1024) / kStageBytes));
   static constexpr int kRedFloats = S::kWarps * S::kRows * (D + 2);
-  static constexpr int kBytes = kStages * kStageBytes + 2 * kStages * 8 + kRedFloats * 4 + 64;
+  static constexpr int kItemSlots = 4;  // whole items handed from the producer to the consumers (dynamic deal)
+  static constexpr int kItemBytes = kItemSlots * 8 * 3 + 8;
+  static constexpr int kBytes = kStages * kStageBytes + 2 * kStages * 8 + kRedFloats * 4 + kItemBytes + 64;
 };
 
 __device__ __forceinline__ void decode_item(long long item, int heads, int splits, int row_blocks,
@@ -178,11 +180,18 @@ __global__ void __launch_bounds__(DecodeShape<D>::kThreads, 1)
   constexpr int kRows = S::kRows;
   constexpr int kStages = M::kStages;
 
+  constexpr int kItemSlots = M::kItemSlots;
+
   extern __shared__ __align__(128) uint8_t smem[];
   T* ring = reinterpret_cast<T*>(smem);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * M::kStageBytes);
   uint64_t* empty = full + kStages;
   float* red = reinterpret_cast<float*>(empty + kStages);
+  // dynamic deal: item indices from the producer to the consumers, and the consumers' shared abort flag
+  long long* item_slot = reinterpret_cast<long long*>(red + M::kRedFloats);
+  uint64_t* item_full = reinterpret_cast<uint64_t*>(item_slot + kItemSlots);
+  uint64_t* item_empty = item_full + kItemSlots;
+  volatile int* item_abort = reinterpret_cast<volatile int*>(item_empty + kItemSlots);
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -192,6 +201,11 @@ __global__ void __launch_bounds__(DecodeShape<D>::kThreads, 1)
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], S::kWarps);
     }
+    for (int i = 0; i < kItemSlots; ++i) {
+      mbar_init(&item_full[i], 1);
+      mbar_init(&item_empty[i], S::kWarps);
+    }
+    *item_abort = 0;
     fence_barrier_init();
   }
   __syncthreads();
@@ -209,7 +223,36 @@ __global__ void __launch_bounds__(DecodeShape<D>::kThreads, 1)
       DecodeCursor cur;
       decode_cursor_init<kContiguous>(a, cur);
       DecodeSegment sg;
-      while (decode_next<D, kContiguous>(a, cur, sg)) {
+      // Dynamic deal (whole items): the items, longest request first with heads innermost, go one at a time to
+      // whichever CTA asks next (a global counter), so the CTAs finish within one item of each other and the
+      // items in flight at any moment are consecutive ones (the heads of a few requests, read together). The
+      // index is drawn one item ahead and handed to the consumers through the item ring.
+      unsigned long long drawn = kContiguous ? 0ull : atomicAdd(&a.ws->next_item, 1ull);
+      uint32_t n_items = 0;
+      while (true) {
+        if constexpr (kContiguous) {
+          if (!decode_next<D, true>(a, cur, sg)) break;
+        } else {
+          const long long item = (ok && drawn < static_cast<unsigned long long>(a.items)) ? static_cast<long long>(drawn)
+                                                                                         : -1ll;
+          if (item >= 0) drawn = atomicAdd(&a.ws->next_item, 1ull);
+          const int slot = n_items % kItemSlots;
+          if (!mbar_wait(&item_empty[slot], ((n_items / kItemSlots) & 1) ^ 1, a.budget_ns)) {
+            ok = false;
+            record_error(a.ws, FGW_ERR_DEVICE_TIMEOUT, 3);
+            break;  // unpublished: the consumers' bounded wait for this slot gives up
+          }
+          item_slot[slot] = item;
+          mbar_arrive(&item_full[slot]);
+          ++n_items;
+          if (item < 0) break;
+          sg.item = item;
+          sg.first = 0;
+          sg.count = -1;
+          sg.piece = false;
+          sg.item_u = 0;
+          sg.units = 0;
+        }
         int b, rb, s, h;
         decode_item(sg.item, a.heads, a.splits, a.row_blocks, a.order, b, rb, s, h);
         const int len = a.lengths[b];
@@ -241,6 +284,14 @@ __global__ void __launch_bounds__(DecodeShape<D>::kThreads, 1)
           }
         }
       }
+      if constexpr (!kContiguous) {
+        // The CTA that draws last resets the deal for the next launch (the plan launch also zeroes it).
+        __threadfence();
+        if (atomicAdd(&a.ws->finished, 1u) == gridDim.x - 1) {
+          a.ws->next_item = 0ull;
+          a.ws->finished = 0u;
+        }
+      }
       // Leave no copy in flight: wait for the stages still owed to the consumers.
       if (!ok) {
         for (uint32_t j = 0; j < (uint32_t)kStages && j < it; ++j) {
@@ -264,7 +315,35 @@ __global__ void __launch_bounds__(DecodeShape<D>::kThreads, 1)
   DecodeCursor cur;
   decode_cursor_init<kContiguous>(a, cur);
   DecodeSegment sg;
-  while (decode_next<D, kContiguous>(a, cur, sg)) {
+  uint32_t n_items = 0;
+  while (true) {
+    if constexpr (kContiguous) {
+      if (!decode_next<D, true>(a, cur, sg)) break;
+    } else {
+      // The next item from the producer. Every consumer warp leaves or stays together (the item loop has
+      // consumer-wide named barriers): a warp whose bounded wait gave up raises the shared abort flag before
+      // the barrier, and all of them read the flag after it.
+      const int slot = n_items % kItemSlots;
+      const bool seen = mbar_wait(&item_full[slot], (n_items / kItemSlots) & 1, a.budget_ns);
+      if (!__all_sync(0xffffffffu, seen) && lane == 0) {
+        *item_abort = 1;
+        record_error(a.ws, FGW_ERR_DEVICE_TIMEOUT, 4);
+      }
+      __syncwarp();
+      named_barrier_sync(2, consumer_threads);
+      const long long item = *item_abort ? -1ll : *reinterpret_cast<volatile long long*>(&item_slot[slot]);
+      __syncwarp();
+      named_barrier_sync(2, consumer_threads);  // every warp has read the flag before any can raise it again
+      if (lane == 0) mbar_arrive(&item_empty[slot]);
+      ++n_items;
+      if (item < 0) break;
+      sg.item = item;
+      sg.first = 0;
+      sg.count = -1;
+      sg.piece = false;
+      sg.item_u = 0;
+      sg.units = 0;
+    }
     int b, rb, s, h;
     decode_item(sg.item, a.heads, a.splits, a.row_blocks, a.order, b, rb, s, h);
     const int len = a.lengths[b];

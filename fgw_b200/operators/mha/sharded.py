@@ -56,8 +56,9 @@ def batch_bins(lengths, world, sq=1, causal=False):
 
 
 def assemble_heads(parts):
-    """O[B, Sq, H, D] from the per-rank outputs [G][B, Sq, H / G, D] of a head-sharded call."""
-    stacked = torch.stack(list(parts))  # [G, B, Sq, Hr, D]
+    """O[B, Sq, H, D] from the per-rank outputs of a head-sharded call: a list [G][B, Sq, H / G, D], or those
+    stacked in one tensor [G, B, Sq, H / G, D] (one copy either way)."""
+    stacked = parts if isinstance(parts, torch.Tensor) else torch.stack(list(parts))  # [G, B, Sq, Hr, D]
     g, b, sq, hr, d = stacked.shape
     return stacked.permute(1, 2, 0, 3, 4).reshape(b, sq, g * hr, d)
 
@@ -74,11 +75,12 @@ def assemble_batch(parts, bins, batch):
 
 
 def _all_gather(local, group, world):
-    """[world] tensors of ``local``'s shape, rank order, over ``group`` (one all-gather)."""
+    """``local`` of every rank over ``group`` (one all-gather), rank order: one stacked tensor on NCCL, a list
+    otherwise."""
     if dist.get_backend(group) == "nccl":
         buf = local.new_empty((world,) + tuple(local.shape))
         dist.all_gather_into_tensor(buf, local.contiguous(), group=group)
-        return list(buf.unbind(0))
+        return buf
     parts = [torch.empty_like(local) for _ in range(world)]
     dist.all_gather(parts, local.contiguous(), group=group)
     return parts
@@ -101,6 +103,15 @@ def mha_paged_decode_sharded(q, k_cache, v_cache, block_table, cache_seqlens, pa
     rank = dist.get_rank(group) if dist.is_initialized() else 0
     if shard == "batch" and gather and (bins is None or len(bins) != world or len(bins[rank]) != q.shape[0]):
         raise ValueError("a gathered batch-sharded call needs every rank's bin, this rank's matching q")
+    if (gather and world > 1 and shard == "heads" and kwargs.get("out") is None
+            and dist.get_backend(group) == "nccl"):
+        # The forward writes straight into this rank's slot of the gather buffer and the all-gather runs in
+        # place, so the only copy is the one that interleaves the ranks' heads into O[B, Sq, H, D].
+        buf = q.new_empty((world,) + tuple(q.shape))
+        kwargs = dict(kwargs, out=buf[rank])
+        mha_paged_decode(q, k_cache, v_cache, block_table, cache_seqlens, page_size, is_causal, **kwargs)
+        dist.all_gather_into_tensor(buf, buf[rank], group=group)
+        return assemble_heads(buf)
     local = mha_paged_decode(q, k_cache, v_cache, block_table, cache_seqlens, page_size, is_causal, **kwargs)
     if not gather or world == 1:
         return local

@@ -72,9 +72,10 @@ typedef enum fgw_path {
 /*
  * How the main launch divides the work between its persistent CTAs (the reference's task_assignment,
  * v7.py:112-113, 260-270, and its static host stream plan, operators/mha/static_schedule.py:48-80, 195-247).
- *   STRIDED:    whole work items (request, head, split, query block) in longest-request-first order, dealt to
- *               the CTAs in snake order: round r gives CTA i item r * grid + i (r even) or r * grid + grid - 1 - i
- *               (r odd), which keeps every CTA's load near the mean with few items per CTA.
+ *   STRIDED:    whole work items (request, head, split, query block) in longest-request-first order. The decode
+ *               kernel deals them dynamically: a counter in the workspace hands the next item to whichever CTA
+ *               asks, so CTAs finish within one item of each other. The tensor kernels deal them in snake
+ *               order: round r gives CTA i item r * grid + i (r even) or r * grid + grid - 1 - i (r odd).
  *   CONTIGUOUS: the KV tiles of all work items, laid end to end, are cut into one contiguous range per CTA
  *               of equal length (loads differ by at most one tile); an item cut between CTAs is computed in
  *               pieces whose partial results the CTA finishing last merges in the same launch.
