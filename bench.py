@@ -24,6 +24,7 @@ reference restated in NumPy (``oracle/``; the reference itself is Python on an A
 run here), on the same headline workload, rank 0 only.
 """
 import argparse
+import contextlib
 import json
 import math
 import os
@@ -64,7 +65,8 @@ def parse_args(argv=None):
                    help="tcgen05 kernel of the long-query workloads")
     p.add_argument("--task-assignment", choices=["strided", "contiguous", "tail"], default=None,
                    help="schedule of the long-query workloads (default: the library's choice)")
-    p.add_argument("--only", choices=["longq", "decode"], default=None, help="measure one workload (profiling)")
+    p.add_argument("--only", choices=["longq", "decode", "d256"], default=None,
+                   help="measure one workload (profiling): config 2, config 5, or config 2's shape at D = 256")
     p.add_argument("--decode-batch", type=int, default=DECODE["batch"],
                    help="requests in the decode workload (smaller values make profiling captures small)")
     return p.parse_args(argv)
@@ -121,6 +123,37 @@ def head_shard(heads, rank, world):
     return rank * per, per
 
 
+@contextlib.contextmanager
+def local_host_memory(device):
+    """Pinned host buffers made inside this block land on the GPU's own NUMA node: the process runs on the CPUs
+    NVML reports as closest to the GPU while they are allocated (the pages are placed where they are first
+    touched), and its CPU affinity is restored afterwards. Host-to-device copies from a remote node cross the
+    inter-socket link, which several ranks then share. Does nothing where NVML or the affinity call is missing."""
+    saved = None
+    try:
+        import pynvml
+        pynvml.nvmlInit()
+        try:
+            prop = torch.cuda.get_device_properties(device)
+            bus = f"{prop.pci_domain_id:08x}:{prop.pci_bus_id:02x}:{prop.pci_device_id:02x}.0"
+            handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            words = pynvml.nvmlDeviceGetCpuAffinity(handle, ((os.cpu_count() or 64) + 63) // 64)
+        finally:
+            pynvml.nvmlShutdown()
+        cpus = {64 * w + bit for w, word in enumerate(words) for bit in range(64) if (word >> bit) & 1}
+        current = os.sched_getaffinity(0)
+        if cpus & current:
+            saved = current
+            os.sched_setaffinity(0, cpus & current)
+    except Exception:  # no NVML, no such device, or no affinity control: allocate where we are
+        saved = None
+    try:
+        yield
+    finally:
+        if saved is not None:
+            os.sched_setaffinity(0, saved)
+
+
 def measured_peaks():
     path = ROOT / "MEASURED_PEAKS.json"
     if path.exists():
@@ -130,13 +163,16 @@ def measured_peaks():
 
 
 # ---------------------------------------------------------------------------------------------- inputs
-def longq_inputs(seed, device, sq=None):
-    c = dict(LONGQ, sq=sq or LONGQ["sq"])
+def longq_inputs(seed, device, sq=None, **shape):
+    """Config 2's inputs (``shape`` overrides batch / heads / dim / kv / page; ``pool_pages`` draws the table from
+    a larger pool, as config 1's 16 of 64 pages)."""
+    c = dict(LONGQ, sq=sq or LONGQ["sq"], **{k: v for k, v in shape.items() if k != "pool_pages"})
     width = c["kv"] // c["page"]
     gen = torch.Generator().manual_seed(seed)
-    table = torch.randperm(c["batch"] * width, generator=gen).reshape(c["batch"], width).to(torch.int32)
+    pool_pages = shape.get("pool_pages", c["batch"] * width)
+    table = torch.randperm(pool_pages, generator=gen)[: c["batch"] * width].reshape(c["batch"], width).to(torch.int32)
     lengths = torch.full((c["batch"],), c["kv"], dtype=torch.int32)
-    pool_rows = c["batch"] * width * c["page"]
+    pool_rows = pool_pages * c["page"]
     gdev = torch.Generator(device=device).manual_seed(seed)
     q = torch.randn(c["batch"], c["sq"], c["heads"], c["dim"], generator=gdev, device=device).to(torch.bfloat16)
     k = torch.randn(pool_rows, c["heads"], c["dim"], generator=gdev, device=device).to(torch.bfloat16)
@@ -331,9 +367,11 @@ def run_longq(args, rank, world, device, stream):
         protocol[name + "_us_median"] = statistics.median(samples) * 1e3
 
     # End to end through the public API: pinned host inputs -> device -> forward -> host output, every step.
-    host = {k: inp[k].cpu().pin_memory() for k in ("q", "k", "v", "table", "lengths")}
+    with local_host_memory(device):
+        host = {k: inp[k].cpu().pin_memory() for k in ("q", "k", "v", "table", "lengths")}
+        host_out = torch.empty(inp["q"].shape, dtype=inp["q"].dtype, pin_memory=True)
+        host_outs = [torch.empty(inp["q"].shape, dtype=inp["q"].dtype, pin_memory=True) for _ in range(2)]
     dev_bufs = {k: torch.empty_like(inp[k]) for k in host}
-    host_out = torch.empty(inp["q"].shape, dtype=inp["q"].dtype, pin_memory=True)
 
     def forward(bufs, out_buf):
         return mha_paged_decode(bufs["q"], bufs["k"], bufs["v"], bufs["table"], bufs["lengths"], c["page"], False,
@@ -352,7 +390,6 @@ def run_longq(args, rank, world, device, stream):
     # i + 1's upload overlaps step i's forward and download (the two copy directions use different engines).
     sets = [{k: torch.empty_like(inp[k]) for k in host} for _ in range(2)]
     outs = [torch.empty_like(inp["q"]) for _ in range(2)]
-    host_outs = [torch.empty(inp["q"].shape, dtype=inp["q"].dtype, pin_memory=True) for _ in range(2)]
     s_up, s_comp, s_down = (torch.cuda.Stream(device) for _ in range(3))
     uploaded, computed, downloaded = ([torch.cuda.Event() for _ in range(2)] for _ in range(3))
 
@@ -399,12 +436,13 @@ def run_longq(args, rank, world, device, stream):
             "launches_per_step": len(fns)}
 
 
-def run_longq_32k(args, rank, world, device, stream):
-    """Config 2's second size (Q = 32768, KV 2048): plan + attend per step with the L2 flushed, per-stage events."""
+def run_longq_shape(args, rank, world, device, stream, seed, sq, steps=None, **shape):
+    """One more long-query (or config-1) shape: plan + attend per step with the L2 flushed, per-stage events; and the
+    same step replayed as a CUDA graph (what a serving loop that captures its launches pays per call)."""
     from fgw_b200.operators.mha.current import build_kernel
-    c = dict(LONGQ, sq=32768)
-    inp = longq_inputs(2000 + rank, device, sq=c["sq"])
-    kernel = build_kernel(c["batch"], c["sq"], c["heads"], c["dim"], inp["k"].shape[0], inp["width"], c["page"],
+    c = dict(LONGQ, sq=sq, **{k: v for k, v in shape.items() if k != "pool_pages"})
+    inp = longq_inputs(seed + rank, device, sq=sq, **shape)
+    kernel = build_kernel(c["batch"], sq, c["heads"], c["dim"], inp["k"].shape[0], inp["width"], c["page"],
                           False, "bfloat16", device.index, num_splits=args.splits, full_kv_cache=True, path=args.path,
                           tensor_kernel=args.tensor_kernel)
     ws = kernel.new_workspace(device)
@@ -416,14 +454,36 @@ def run_longq_32k(args, rank, world, device, stream):
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=device)
     barrier(world)
     torch.cuda.synchronize()
-    steps = max(3, args.steps // 4)
+    steps = steps or max(3, args.steps // 4)
     per, totals = timed_steps(fns, steps, 3, flush, stream)
+    # the same step as a CUDA graph (captured as the headline's is), L2 flushed before each replay
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream(device)
+    side.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(side):
+        for _, fn in fns:
+            fn()
+    torch.cuda.current_stream(device).wait_stream(side)
+    with torch.cuda.graph(graph):
+        for _, fn in fns:
+            fn()
     torch.cuda.synchronize()
+    _, graph_ms = timed_steps([("step", graph.replay)], steps, 3, flush, stream)
+    torch.cuda.synchronize()
+    del graph
     barrier(world)
     ok = check_longq(inp, out)
-    return {"flops": flops_of(inp, c["sq"], c["heads"], c["dim"]), "step_ms": sum(totals) / len(totals),
-            "attend_ms": sum(per["attend"]) / len(per["attend"]), "parity": ok, "launches": len(fns) * steps,
-            "num_splits": kernel.num_splits, "task_assignment": kernel.task_assignment}
+    return {"flops": flops_of(inp, sq, c["heads"], c["dim"]),
+            "bytes": bytes_of(inp, c["batch"], sq, c["heads"], c["dim"]),
+            "step_ms": sum(totals) / len(totals), "graph_ms": statistics.median(graph_ms),
+            "attend_ms": sum(per["attend"]) / len(per["attend"]), "parity": ok,
+            "launches": len(fns) * steps * 2, "num_splits": kernel.num_splits,
+            "task_assignment": kernel.task_assignment, "execution_path": kernel.execution_path}
+
+
+def run_longq_32k(args, rank, world, device, stream):
+    """Config 2's second size (Q = 32768, KV 2048)."""
+    return run_longq_shape(args, rank, world, device, stream, 2000, 32768)
 
 
 def torch_reference(q, keys, values, scale):
@@ -441,7 +501,7 @@ def live_rows(table_row, length, page, device):
 def check_longq(inp, out):
     """Spot check of the benchmarked output (first request, first 256 query rows) against a PyTorch FP32
     reference of the same attention."""
-    rows = 256
+    rows = min(256, out.shape[1])
     idx = live_rows(inp["table"][0], inp["host_lengths"][0], inp["page"], out.device)
     want = torch_reference(inp["q"][0, :rows], inp["k"][idx], inp["v"][idx], inp["q"].shape[-1] ** -0.5)
     err = float((out[0, :rows].float() - want).abs().max())
@@ -493,9 +553,10 @@ def run_decode_serving(args, dc, rank, world, device, stream):
     inp = dc["inp"]
     steps = max(10, args.steps)
     base = np.asarray(inp["host_lengths"], dtype=np.int32)  # the cache_seqlens dtype, kept on the host as well
-    host_q = inp["q"].cpu().pin_memory()
-    host_len = torch.empty(base.shape[0], dtype=torch.int32).pin_memory()
-    host_out = torch.empty(inp["q"].shape, dtype=inp["q"].dtype).pin_memory()
+    with local_host_memory(device):
+        host_q = inp["q"].cpu().pin_memory()
+        host_len = torch.empty(base.shape[0], dtype=torch.int32).pin_memory()
+        host_out = torch.empty(inp["q"].shape, dtype=inp["q"].dtype).pin_memory()
     dev_q, dev_len = torch.empty_like(inp["q"]), torch.empty_like(inp["lengths"])
     out = torch.empty_like(inp["q"])
     schedule = [np.maximum(base - (steps + 3 - i), 1) for i in range(steps + 3)]  # grows to the config's lengths
@@ -864,7 +925,8 @@ def main(argv=None):
         achieved = lq32["flops"] / (lq32["attend_ms"] * 1e-3) / 1e12
         line["longq_q32768"] = {
             "workload": "longq_b2h8_q32768_kv2048_bf16_d128_page128", "scaling": "weak",
-            "us_per_call": step_ms32 * 1e3, "unit": "TFLOP/s",
+            "us_per_call": step_ms32 * 1e3, "graph_us_per_call": max_over_ranks(lq32["graph_ms"], world) * 1e3,
+            "unit": "TFLOP/s",
             "value": sum_over_ranks(lq32["flops"], world) / (step_ms32 * 1e-3) / 1e12,
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": tc_peak, "unit": "TFLOP/s",
                          "frac": achieved / tc_peak, "kernel": "attend", "peak_source": f"{peak_kind} bf16_tflops"},
@@ -872,6 +934,47 @@ def main(argv=None):
             "l2": "flushed (256 MiB write) before every step; eager plan + attend, per-stage events",
             "parity": lq32["parity"], "gpu_launches": lq32["launches"]}
         line["gpu_launches"] = line.get("gpu_launches", 0) + lq32["launches"]
+    if args.only in (None, "d256"):
+        # more shapes of BASELINE's configurations, weak-scaled like the headline (every rank its own call)
+        extra = [
+            ("config1", "decode_b1h1_q1_kv2048_bf16_d128_page128_16of64", "hbm",
+             dict(seed=3000, sq=1, steps=max(10, args.steps), batch=1, heads=1, pool_pages=64), 32.9),
+            ("b1h1_q32768", "longq_b1h1_q32768_kv2048_bf16_d128_page128", "tensor",
+             dict(seed=3100, sq=32768, batch=1, heads=1), 175.0),
+            ("longq_d256", "longq_b2h8_q4096_kv2048_bf16_d256_page128", "tensor",
+             dict(seed=3200, sq=4096, dim=256), None),
+        ]
+        if args.only == "d256":
+            extra = extra[2:]
+        for key, workload, bound, shape, published in extra:
+            r = run_longq_shape(args, rank, world, device, stream, **shape)
+            ms = max_over_ranks(r["step_ms"], world)
+            graph_ms = max_over_ranks(r["graph_ms"], world)
+            if bound == "tensor":
+                achieved = r["flops"] / (r["attend_ms"] * 1e-3) / 1e12
+                roof = {"bound": "tensor", "achieved": achieved, "peak": tc_peak, "unit": "TFLOP/s",
+                        "frac": achieved / tc_peak, "kernel": "attend (" + r["execution_path"] + ")",
+                        "peak_source": f"{peak_kind} bf16_tflops"}
+                value, unit = sum_over_ranks(r["flops"], world) / (ms * 1e-3) / 1e12, "TFLOP/s"
+            else:
+                achieved = r["bytes"] / (r["attend_ms"] * 1e-3) / 1e9
+                roof = {"bound": "hbm (launch-bound in practice)", "achieved": achieved, "peak": hbm_peak,
+                        "unit": "GB/s", "frac": achieved / hbm_peak, "kernel": "attend (" + r["execution_path"] + ")",
+                        "peak_source": f"{peak_kind} hbm_gbs"}
+                value, unit = sum_over_ranks(r["bytes"], world) / (ms * 1e-3) / 1e9, "GB/s"
+            line[key] = {"workload": workload, "scaling": "weak", "us_per_call": ms * 1e3,
+                         "graph_us_per_call": graph_ms * 1e3, "value": value, "unit": unit, "roofline": roof,
+                         "num_splits": r["num_splits"], "task_assignment": r["task_assignment"],
+                         "l2": "flushed (256 MiB write) before every step; eager plan + attend with per-stage "
+                               "events, and the same step replayed as a CUDA graph",
+                         "parity": r["parity"], "gpu_launches": r["launches"]}
+            if published is not None:
+                line[key]["published_ascend_us"] = published
+            line["gpu_launches"] = line.get("gpu_launches", 0) + r["launches"]
+        if lq is None:
+            d = line["longq_d256"]
+            line.update({"value": d["value"], "unit": d["unit"], "ms_per_step": d["us_per_call"] / 1e3,
+                         "vs_baseline": None, "config": {"workload": d["workload"]}, "roofline": d["roofline"]})
     if args.only is None:
         st = run_longq_strong(args, rank, world, device, stream)
         local_ms = max_over_ranks(st["local_ms"], world)

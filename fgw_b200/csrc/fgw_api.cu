@@ -31,6 +31,61 @@ EncodeTiledFn encode_tiled() {
   return fn;
 }
 
+CUresult encode_tiled_cached(CUtensorMap* map, CUtensorMapDataType dtype, cuuint32_t rank, void* base,
+                             const cuuint64_t* dims, const cuuint64_t* strides, const cuuint32_t* box,
+                             const cuuint32_t* elem_strides, CUtensorMapInterleave interleave,
+                             CUtensorMapSwizzle swizzle, CUtensorMapL2promotion l2, CUtensorMapFloatOOBfill fill) {
+  struct Key {
+    void* base;
+    cuuint64_t dims[5], strides[4];
+    cuuint32_t box[5], elem_strides[5];
+    int dtype, rank, interleave, swizzle, l2, fill;
+    bool operator==(const Key& o) const { return std::memcmp(this, &o, sizeof(Key)) == 0; }
+  };
+  struct Entry {
+    Key key;
+    CUtensorMap map;
+  };
+  constexpr int kEntries = 32;
+  static std::mutex mu;
+  static Entry cache[kEntries];
+  static int used = 0, next = 0;
+  if (rank < 1 || rank > 5) return CUDA_ERROR_INVALID_VALUE;
+  Key k;
+  std::memset(&k, 0, sizeof(k));
+  k.base = base;
+  for (cuuint32_t i = 0; i < rank; ++i) {
+    k.dims[i] = dims[i];
+    k.box[i] = box[i];
+    k.elem_strides[i] = elem_strides[i];
+    if (i + 1 < rank) k.strides[i] = strides[i];
+  }
+  k.dtype = dtype;
+  k.rank = static_cast<int>(rank);
+  k.interleave = interleave;
+  k.swizzle = swizzle;
+  k.l2 = l2;
+  k.fill = fill;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    for (int i = 0; i < used; ++i) {
+      if (cache[i].key == k) {
+        *map = cache[i].map;
+        return CUDA_SUCCESS;
+      }
+    }
+  }
+  const CUresult r = encode_tiled()(map, dtype, rank, base, dims, strides, box, elem_strides, interleave, swizzle,
+                                    l2, fill);
+  if (r != CUDA_SUCCESS) return r;
+  std::lock_guard<std::mutex> lock(mu);
+  cache[next].key = k;
+  cache[next].map = *map;
+  next = (next + 1) % kEntries;
+  used = used < kEntries ? used + 1 : kEntries;
+  return CUDA_SUCCESS;
+}
+
 // The tcgen05 kernel the tensor path runs for these parameters (FGW_TENSOR_KERNEL_AUTO resolved).
 int resolve_tensor_kernel(const fgw_mha_params& p) {
   if (p.tensor_kernel != FGW_TENSOR_KERNEL_AUTO) return p.tensor_kernel;

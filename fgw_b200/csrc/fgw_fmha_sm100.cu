@@ -510,7 +510,7 @@ static bool make_q_map(CUtensorMap* map, const fgw_mha_params& p) {
   const cuuint32_t estride[4] = {1, 1, 1, 1};
   const CUtensorMapDataType dt =
       p.dtype == FGW_DTYPE_BFLOAT16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  return encode_tiled()(map, dt, 4, const_cast<void*>(p.q), dims, strides, box, estride,
+  return encode_tiled_cached(map, dt, 4, const_cast<void*>(p.q), dims, strides, box, estride,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -522,7 +522,7 @@ static bool make_kv_sw_map(CUtensorMap* map, const void* base, const fgw_mha_par
   const cuuint32_t estride[3] = {1, 1, 1};
   const CUtensorMapDataType dt =
       p.dtype == FGW_DTYPE_BFLOAT16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  return encode_tiled()(map, dt, 3, const_cast<void*>(base), dims, strides, box, estride,
+  return encode_tiled_cached(map, dt, 3, const_cast<void*>(base), dims, strides, box, estride,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }

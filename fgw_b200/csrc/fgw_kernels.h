@@ -102,5 +102,12 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 EncodeTiledFn encode_tiled();
+// cuTensorMapEncodeTiled through a small cache of recent descriptors: a serving loop encodes the same K/V pool
+// maps every call, and a descriptor depends only on these arguments (no device state), so a hit skips the
+// driver call.
+CUresult encode_tiled_cached(CUtensorMap* map, CUtensorMapDataType dtype, cuuint32_t rank, void* base,
+                             const cuuint64_t* dims, const cuuint64_t* strides, const cuuint32_t* box,
+                             const cuuint32_t* elem_strides, CUtensorMapInterleave interleave,
+                             CUtensorMapSwizzle swizzle, CUtensorMapL2promotion l2, CUtensorMapFloatOOBfill fill);
 
 }  // namespace fgw

@@ -20,6 +20,7 @@ callable; the CUDA kernels size their own TMA rings, so they do not change the s
 ``persistent_programs`` caps the persistent grid (default: the SM count; ``None`` uncapped).
 """
 import functools
+import threading
 
 import numpy as np
 import torch
@@ -93,6 +94,9 @@ def _native_split_model():
 
 
 _route_cached = functools.lru_cache(maxsize=64)(route)
+
+_KEPT_WORKSPACE_BYTES = 64 << 20  # a launcher keeps workspaces up to this size between eager calls
+_KEPT_WORKSPACES = 8              # (device, stream) pairs per launcher
 
 
 def _current_stream(device):
@@ -286,10 +290,29 @@ def build_kernel(batch, sq, heads, dim, pool_rows, width, page_size, causal, dty
     def _workspace(device):
         return torch.empty(max(workspace_bytes, 256), dtype=torch.uint8, device=device)
 
+    # Workspaces of eager calls that pass none, kept per (device, stream): calls on one stream run in order, so
+    # the next call may reuse the workspace (the plan launch re-initialises what the kernels read), and a
+    # serving loop saves an allocation per call. A call being captured into a CUDA graph gets a workspace of its
+    # own (the graph keeps it), and large workspaces (many splits) are not kept.
+    kept = {}
+    kept_lock = threading.Lock()
+    keep = workspace_bytes <= _KEPT_WORKSPACE_BYTES
+
     def launch(q, k, v, table, lengths, out=None, workspace=None):
         out = torch.empty_like(q) if out is None else out
-        ws = _workspace(q.device) if workspace is None else workspace
-        _native.paged_fwd(_bind(q, k, v, table, lengths, out), ws.data_ptr(), ws.numel(), _current_stream(q.get_device()))
+        device = q.get_device()
+        stream = _current_stream(device)
+        if workspace is not None or not keep or torch.cuda.is_current_stream_capturing():
+            ws = _workspace(q.device) if workspace is None else workspace
+            _native.paged_fwd(_bind(q, k, v, table, lengths, out), ws.data_ptr(), ws.numel(), stream)
+            return out
+        with kept_lock:  # one enqueue at a time per kept workspace (ctypes releases the GIL in the call)
+            ws = kept.get((device, stream))
+            if ws is None:
+                if len(kept) >= _KEPT_WORKSPACES:
+                    kept.clear()
+                ws = kept[(device, stream)] = _workspace(q.device)
+            _native.paged_fwd(_bind(q, k, v, table, lengths, out), ws.data_ptr(), ws.numel(), stream)
         return out
 
     def plan_kernel(q, k, v, table, lengths, workspace):
