@@ -625,27 +625,37 @@ __global__ void __launch_bounds__(384, 1)
         // its program's slot (2 p for the piece a program starts with, 2 p + 1 for the one it ends with), then
         // counts itself in on the item's arrival counter; the piece whose count completes the set merges all
         // pieces from their slots in piece order, so the result does not depend on which CTA finished last.
-        // No CTA ever waits for another.
+        // No CTA ever waits for another. A slot holds O column by column ([D][256 rows]), so the 32 rows of a
+        // warp write, and read back, 128 contiguous bytes per column.
         const long long total = a.prog_u[a.programs];
         const int q_first = program_of(total, a.programs, sg.item_u);
         const int pieces = program_of(total, a.programs, sg.item_u + sg.units - 1) - q_first + 1;
         const int first_extra = sg.item_u != program_start(total, a.programs, q_first) ? 1 : 0;
         const int own = blockIdx.x - q_first;
-        // slot row of piece k, relative to piece 0's (piece k >= 1 sits 2k - first_extra slots later)
-        auto piece_row = [&](int k) -> long long {
-          return (2ll * q_first + first_extra + (k == 0 ? 0 : 2 * k - first_extra)) * kPairRows + 128 * t + row;
+        const int r = 128 * t + row;  // this thread's row in the pair item
+        // slot of piece k (piece k >= 1 sits 2k - first_extra slots after piece 0's)
+        auto piece_slot = [&](int k) -> long long {
+          return 2ll * q_first + first_extra + (k == 0 ? 0 : 2 * k - first_extra);
         };
-        const long long my_row = piece_row(own);
+        auto slot_column = [&](long long slot, int d) -> float* {
+          return a.slot_o + (slot * D + d) * kPairRows + r;
+        };
+        const long long my_slot = piece_slot(own);
         for (int cb = 0; cb < D / 16; ++cb) {
           float o[16];
           load_o(cb, o);  // warp-collective: every lane, valid row or not
           if (row_valid) {
-            float4* dst = reinterpret_cast<float4*>(a.slot_o + my_row * D + cb * 16);
 #pragma unroll
-            for (int i = 0; i < 4; ++i) dst[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+            for (int i = 0; i < 16; ++i) *slot_column(my_slot, cb * 16 + i) = o[i];
           }
         }
-        if (row_valid) a.slot_lse[my_row] = own_lse;
+        if (row_valid) a.slot_lse[my_slot * kPairRows + r] = own_lse;
+        // O_t is out of TMEM: the next segment's first PV may overwrite it while this piece counts in and merges
+        if (n_t > 0) {
+          tc_fence_before_sync();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&o_empty[t]);
+        }
         named_barrier_sync(1, 256);  // both warpgroups have written their rows
         if (warp == 4 && lane == 0) {
           __threadfence();
@@ -657,13 +667,29 @@ __global__ void __launch_bounds__(384, 1)
         if (merge) {
           __threadfence();
           if (warp == 4 && lane == 0) a.counters[sg.item] = 0;  // ready for the next launch
-          // base-2 LSE merge (the split merge's arithmetic, merge_kernel in fgw_aux.cu)
+          // base-2 LSE merge (the split merge's arithmetic, merge_kernel in fgw_aux.cu): the weights of the
+          // first kKeep pieces stay in registers, and every piece's loads of a column block are independent, so
+          // they are in flight together instead of one dependent round trip per piece and block
           if (row_valid) {
+            constexpr int kKeep = 8;
+            auto lse_of = [&](int k) { return __ldcg(&a.slot_lse[piece_slot(k) * kPairRows + r]); };
             float peak = kEmptyLse;
-            for (int k = 0; k < pieces; ++k) peak = fmaxf(peak, __ldcg(&a.slot_lse[piece_row(k)]));
+            for (int k = 0; k < pieces; ++k) peak = fmaxf(peak, lse_of(k));
+            float w[kKeep];
             float wsum = 0.f;
-            for (int k = 0; k < pieces; ++k) {
-              const float lse = __ldcg(&a.slot_lse[piece_row(k)]);
+#pragma unroll
+            for (int k = 0; k < kKeep; ++k) {
+              w[k] = 0.f;
+              if (k < pieces) {
+                const float lse = lse_of(k);
+                if (lse > kValidLse) {
+                  w[k] = fast_exp2(lse - peak);
+                  wsum += w[k];
+                }
+              }
+            }
+            for (int k = kKeep; k < pieces; ++k) {
+              const float lse = lse_of(k);
               if (lse > kValidLse) wsum += fast_exp2(lse - peak);
             }
             const float scale = wsum > 0.f ? 1.f / wsum : 0.f;
@@ -671,25 +697,27 @@ __global__ void __launch_bounds__(384, 1)
               float acc[16];
 #pragma unroll
               for (int i = 0; i < 16; ++i) acc[i] = 0.f;
-              for (int k = 0; k < pieces; ++k) {
-                const long long pr = piece_row(k);
-                const float lse = __ldcg(&a.slot_lse[pr]);
-                if (!(lse > kValidLse)) continue;
-                const float w = fast_exp2(lse - peak);
-                const float4* src = reinterpret_cast<const float4*>(a.slot_o + pr * D + cb * 16);
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                  const float4 v = __ldcg(src + i);
-                  acc[4 * i] += w * v.x;
-                  acc[4 * i + 1] += w * v.y;
-                  acc[4 * i + 2] += w * v.z;
-                  acc[4 * i + 3] += w * v.w;
+              for (int k = 0; k < kKeep; ++k) {
+                if (k < pieces && w[k] != 0.f) {
+                  const long long slot = piece_slot(k);
+#pragma unroll
+                  for (int i = 0; i < 16; ++i) acc[i] = fmaf(w[k], __ldcg(slot_column(slot, cb * 16 + i)), acc[i]);
                 }
+              }
+              for (int k = kKeep; k < pieces; ++k) {
+                const float lse = lse_of(k);
+                if (!(lse > kValidLse)) continue;
+                const float wk = fast_exp2(lse - peak);
+                const long long slot = piece_slot(k);
+#pragma unroll
+                for (int i = 0; i < 16; ++i) acc[i] = fmaf(wk, __ldcg(slot_column(slot, cb * 16 + i)), acc[i]);
               }
               store_row(cb, acc, scale);
             }
           }
         }
+        continue;  // this segment's O_t was released above
       }
       if (n_t > 0) {
         tc_fence_before_sync();
