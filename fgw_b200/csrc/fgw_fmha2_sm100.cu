@@ -625,8 +625,8 @@ __global__ void __launch_bounds__(384, 1)
         // its program's slot (2 p for the piece a program starts with, 2 p + 1 for the one it ends with), then
         // counts itself in on the item's arrival counter; the piece whose count completes the set merges all
         // pieces from their slots in piece order, so the result does not depend on which CTA finished last.
-        // No CTA ever waits for another. A slot holds O column by column ([D][256 rows]), so the 32 rows of a
-        // warp write, and read back, 128 contiguous bytes per column.
+        // No CTA ever waits for another. A slot holds O in groups of four columns ([D / 4][256 rows][4]), so the
+        // 32 rows of a warp write, and read back, 512 contiguous bytes per group with one 16-byte access each.
         const long long total = a.prog_u[a.programs];
         const int q_first = program_of(total, a.programs, sg.item_u);
         const int pieces = program_of(total, a.programs, sg.item_u + sg.units - 1) - q_first + 1;
@@ -637,8 +637,8 @@ __global__ void __launch_bounds__(384, 1)
         auto piece_slot = [&](int k) -> long long {
           return 2ll * q_first + first_extra + (k == 0 ? 0 : 2 * k - first_extra);
         };
-        auto slot_column = [&](long long slot, int d) -> float* {
-          return a.slot_o + (slot * D + d) * kPairRows + r;
+        auto slot_group = [&](long long slot, int g) -> float4* {  // columns [4 g, 4 g + 4) of this row
+          return reinterpret_cast<float4*>(a.slot_o) + (slot * (D / 4) + g) * kPairRows + r;
         };
         const long long my_slot = piece_slot(own);
         for (int cb = 0; cb < D / 16; ++cb) {
@@ -646,7 +646,9 @@ __global__ void __launch_bounds__(384, 1)
           load_o(cb, o);  // warp-collective: every lane, valid row or not
           if (row_valid) {
 #pragma unroll
-            for (int i = 0; i < 16; ++i) *slot_column(my_slot, cb * 16 + i) = o[i];
+            for (int i = 0; i < 4; ++i) {
+              *slot_group(my_slot, cb * 4 + i) = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+            }
           }
         }
         if (row_valid) a.slot_lse[my_slot * kPairRows + r] = own_lse;
@@ -667,53 +669,53 @@ __global__ void __launch_bounds__(384, 1)
         if (merge) {
           __threadfence();
           if (warp == 4 && lane == 0) a.counters[sg.item] = 0;  // ready for the next launch
-          // base-2 LSE merge (the split merge's arithmetic, merge_kernel in fgw_aux.cu): the weights of the
-          // first kKeep pieces stay in registers, and every piece's loads of a column block are independent, so
-          // they are in flight together instead of one dependent round trip per piece and block
+          // base-2 LSE merge (the split merge's arithmetic, merge_kernel in fgw_aux.cu), in piece order; each
+          // round loads 32 values of every piece with independent 16-byte loads, so a round costs one L2 round
+          // trip per piece instead of one per piece and value
           if (row_valid) {
-            constexpr int kKeep = 8;
             auto lse_of = [&](int k) { return __ldcg(&a.slot_lse[piece_slot(k) * kPairRows + r]); };
             float peak = kEmptyLse;
             for (int k = 0; k < pieces; ++k) peak = fmaxf(peak, lse_of(k));
-            float w[kKeep];
             float wsum = 0.f;
-#pragma unroll
-            for (int k = 0; k < kKeep; ++k) {
-              w[k] = 0.f;
-              if (k < pieces) {
-                const float lse = lse_of(k);
-                if (lse > kValidLse) {
-                  w[k] = fast_exp2(lse - peak);
-                  wsum += w[k];
-                }
-              }
-            }
-            for (int k = kKeep; k < pieces; ++k) {
+            for (int k = 0; k < pieces; ++k) {
               const float lse = lse_of(k);
               if (lse > kValidLse) wsum += fast_exp2(lse - peak);
             }
             const float scale = wsum > 0.f ? 1.f / wsum : 0.f;
-            for (int cb = 0; cb < D / 16; ++cb) {
-              float acc[16];
+            // two column blocks (32 values) per round; a piece's weight is reloaded with its values, so nothing
+            // is indexed by piece in registers
+            auto piece_weight = [&](int k) -> float {
+              const float lse = lse_of(k);
+              return lse > kValidLse ? fast_exp2(lse - peak) : 0.f;
+            };
+            for (int cb = 0; cb < D / 16; cb += 2) {
+              const bool second = cb + 1 < D / 16;
+              float acc0[16], acc1[16];
 #pragma unroll
-              for (int i = 0; i < 16; ++i) acc[i] = 0.f;
+              for (int i = 0; i < 16; ++i) acc0[i] = acc1[i] = 0.f;
+              for (int k = 0; k < pieces; ++k) {
+                const float wk = piece_weight(k);
+                if (wk == 0.f) continue;
+                const long long slot = piece_slot(k);
+                float4 v[8];
 #pragma unroll
-              for (int k = 0; k < kKeep; ++k) {
-                if (k < pieces && w[k] != 0.f) {
-                  const long long slot = piece_slot(k);
+                for (int i = 0; i < 8; ++i) {
+                  v[i] = (i < 4 || second) ? __ldcg(slot_group(slot, cb * 4 + i)) : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
 #pragma unroll
-                  for (int i = 0; i < 16; ++i) acc[i] = fmaf(w[k], __ldcg(slot_column(slot, cb * 16 + i)), acc[i]);
+                for (int i = 0; i < 4; ++i) {
+                  acc0[4 * i] = fmaf(wk, v[i].x, acc0[4 * i]);
+                  acc0[4 * i + 1] = fmaf(wk, v[i].y, acc0[4 * i + 1]);
+                  acc0[4 * i + 2] = fmaf(wk, v[i].z, acc0[4 * i + 2]);
+                  acc0[4 * i + 3] = fmaf(wk, v[i].w, acc0[4 * i + 3]);
+                  acc1[4 * i] = fmaf(wk, v[4 + i].x, acc1[4 * i]);
+                  acc1[4 * i + 1] = fmaf(wk, v[4 + i].y, acc1[4 * i + 1]);
+                  acc1[4 * i + 2] = fmaf(wk, v[4 + i].z, acc1[4 * i + 2]);
+                  acc1[4 * i + 3] = fmaf(wk, v[4 + i].w, acc1[4 * i + 3]);
                 }
               }
-              for (int k = kKeep; k < pieces; ++k) {
-                const float lse = lse_of(k);
-                if (!(lse > kValidLse)) continue;
-                const float wk = fast_exp2(lse - peak);
-                const long long slot = piece_slot(k);
-#pragma unroll
-                for (int i = 0; i < 16; ++i) acc[i] = fmaf(wk, __ldcg(slot_column(slot, cb * 16 + i)), acc[i]);
-              }
-              store_row(cb, acc, scale);
+              store_row(cb, acc0, scale);
+              if (second) store_row(cb + 1, acc1, scale);
             }
           }
         }
