@@ -70,6 +70,7 @@ __global__ void __launch_bounds__(1024) plan_kernel(const int32_t* __restrict__ 
                                                    int merge_groups) {
   extern __shared__ unsigned long long keys[];
   __shared__ long long chunk_sum[1024];
+  grid_dependents_launch();  // the attention launch may start its set-up; it waits for this grid to finish
   if (threadIdx.x == 0) {
     ws->error = 0;
     ws->error_site = 0;

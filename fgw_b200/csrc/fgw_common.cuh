@@ -346,6 +346,12 @@ __device__ __forceinline__ void tc_fence_before_sync() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }
 
+// Programmatic dependent launch: a kernel launched with launch_after_plan may start its set-up while the plan
+// kernel before it on the stream still runs; it reads what the plan wrote only after grid_dependency_wait(), which
+// returns once that kernel has completed and its writes are visible. The plan lets its dependent start at once.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dependents_launch() { asm volatile("griddepcontrol.launch_dependents;"); }
+
 __device__ __forceinline__ void tc_fence_after_sync() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }

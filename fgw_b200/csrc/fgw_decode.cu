@@ -209,6 +209,7 @@ __global__ void __launch_bounds__(DecodeShape<D>::kThreads, 1)
     fence_barrier_init();
   }
   __syncthreads();
+  grid_dependency_wait();  // the plan's lengths, order and counters from here on
 
   if (warp == S::kWarps) {
     // ----------------------------------------------------------------- producer warp
@@ -682,8 +683,7 @@ static cudaError_t launch_decode_t(const LaunchDesc& d, const DecodeArgs& args, 
   const long long cap = d.p.grid_cap > 0 ? d.p.grid_cap : d.sm_count;
   grid = args.contiguous ? args.programs : std::min(grid, cap);
   if (grid <= 0) return cudaSuccess;
-  kernel<<<(unsigned)grid, S::kThreads, M::kBytes, d.stream>>>(kmap, vmap, args);
-  return cudaGetLastError();
+  return launch_after_plan(kernel, (unsigned)grid, S::kThreads, M::kBytes, d.stream, kmap, vmap, args);
 }
 
 // Tokens per pipeline stage of the decode kernel for this head dimension (the TMA box rows must divide it).

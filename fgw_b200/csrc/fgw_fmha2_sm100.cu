@@ -255,6 +255,7 @@ __global__ void __launch_bounds__(384, 1)
   tc_fence_after_sync();
   const uint32_t tmem = *tmem_slot;
   const int D = a.dim;
+  grid_dependency_wait();  // the plan's lengths, order and counters from here on
 
   if (warp < 4) setmaxnreg_dec<S::kRegsControl>();  // warpgroup 0: TMA, MMA and two idle warps
   if (warp == 0) {
@@ -754,8 +755,7 @@ static cudaError_t launch_fmha2_t(const LaunchDesc& d, const Fmha2Args& args, co
   const long long grid = args.contiguous ? args.programs
                                          : std::min<long long>(args.items, std::min<long long>(cap, d.sm_count));
   if (grid <= 0) return cudaSuccess;
-  kernel<<<(unsigned)grid, S::kThreads, S::kBytes, d.stream>>>(qmap, kmap, vmap, args);
-  return cudaGetLastError();
+  return launch_after_plan(kernel, (unsigned)grid, S::kThreads, S::kBytes, d.stream, qmap, kmap, vmap, args);
 }
 
 cudaError_t launch_tensor_pairs(const LaunchDesc& d, bool write_partials, const CUtensorMap& qmap,

@@ -152,6 +152,7 @@ __global__ void __launch_bounds__(256, 1)
   const uint32_t tmem = *tmem_slot;
   const int grid = gridDim.x;
   const int D = a.dim;
+  grid_dependency_wait();  // the plan's lengths, order and counters from here on
 
   if (warp == 0) {
     // ------------------------------------------------------------------------- TMA producer
@@ -537,8 +538,8 @@ static cudaError_t launch_tensor_t(const LaunchDesc& d, const TensorArgs& args, 
   const long long cap = d.p.grid_cap > 0 ? d.p.grid_cap : d.sm_count;
   const long long grid = std::min<long long>(args.items, std::min<long long>(cap, d.sm_count));
   if (grid <= 0) return cudaSuccess;
-  kernel<<<(unsigned)grid, TensorShape<NB>::kThreads, L::kBytes, d.stream>>>(qmap, kmap, vmap, args);
-  return cudaGetLastError();
+  return launch_after_plan(kernel, (unsigned)grid, TensorShape<NB>::kThreads, L::kBytes, d.stream, qmap, kmap, vmap,
+                           args);
 }
 
 cudaError_t launch_tensor(const LaunchDesc& d, bool write_partials) {

@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "fgw_mha.h"
 
 namespace fgw {
@@ -61,6 +63,24 @@ int decode_rows_per_item(int head_dim);
 // `smem_bytes` of dynamic shared memory (an attribute of the function in the device's context) and reports the
 // registers per thread the build gave it (`regs` may be null).
 cudaError_t prepare_kernel(const void* kernel, int smem_bytes, int device, int* regs);
+
+// Launch of a kernel that follows the plan kernel on the stream, as a programmatic dependent launch (it may start
+// while the plan finishes; it calls grid_dependency_wait() before reading the plan's results).
+template <typename... KernelArgs, typename... Args>
+cudaError_t launch_after_plan(void (*kernel)(KernelArgs...), unsigned grid, unsigned block, size_t smem,
+                              cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 int decode_tile_tokens(int head_dim);
 // Work items the contiguous schedule lays end to end: the two-tile kernel's on the tensor path, the decode
 // kernel's (request, query-row block, head) on the decode path.
