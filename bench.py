@@ -455,18 +455,22 @@ def run_longq_shape(args, rank, world, device, stream, seed, sq, steps=None, **s
     barrier(world)
     torch.cuda.synchronize()
     steps = steps or max(3, args.steps // 4)
-    per, totals = timed_steps(fns, steps, 3, flush, stream)
-    # the same step as a CUDA graph (captured as the headline's is), L2 flushed before each replay
+    # per-stage events (plan, attend[, merge]) for the attend kernel's roofline
+    per, _ = timed_steps(fns, steps, 3, flush, stream)
+    # the call itself (the launch callable: plan + attend, split partials merged in place on the decode path),
+    # eager and replayed as a CUDA graph (captured as the headline's is), L2 flushed before each
+    call = [("call", lambda: kernel(*a, out=out, workspace=ws))]
+    # launches of one call: plan + attend, plus the merge launch of a split tensor-path call
+    per_call = 2 + (1 if kernel.num_splits > 1 and kernel.execution_path != "sm100_decode" else 0)
+    _, totals = timed_steps(call, steps, 3, flush, stream)
     graph = torch.cuda.CUDAGraph()
     side = torch.cuda.Stream(device)
     side.wait_stream(torch.cuda.current_stream(device))
     with torch.cuda.stream(side):
-        for _, fn in fns:
-            fn()
+        call[0][1]()
     torch.cuda.current_stream(device).wait_stream(side)
     with torch.cuda.graph(graph):
-        for _, fn in fns:
-            fn()
+        call[0][1]()
     torch.cuda.synchronize()
     _, graph_ms = timed_steps([("step", graph.replay)], steps, 3, flush, stream)
     torch.cuda.synchronize()
@@ -477,7 +481,7 @@ def run_longq_shape(args, rank, world, device, stream, seed, sq, steps=None, **s
             "bytes": bytes_of(inp, c["batch"], sq, c["heads"], c["dim"]),
             "step_ms": sum(totals) / len(totals), "graph_ms": statistics.median(graph_ms),
             "attend_ms": sum(per["attend"]) / len(per["attend"]), "parity": ok,
-            "launches": len(fns) * steps * 2, "num_splits": kernel.num_splits,
+            "launches": (len(fns) + 2 * per_call) * steps, "num_splits": kernel.num_splits,
             "task_assignment": kernel.task_assignment, "execution_path": kernel.execution_path}
 
 
@@ -965,8 +969,9 @@ def main(argv=None):
             line[key] = {"workload": workload, "scaling": "weak", "us_per_call": ms * 1e3,
                          "graph_us_per_call": graph_ms * 1e3, "value": value, "unit": unit, "roofline": roof,
                          "num_splits": r["num_splits"], "task_assignment": r["task_assignment"],
-                         "l2": "flushed (256 MiB write) before every step; eager plan + attend with per-stage "
-                               "events, and the same step replayed as a CUDA graph",
+                         "l2": "flushed (256 MiB write) before every step; us_per_call = the launch callable "
+                               "eager, graph_us_per_call = the same call replayed as a CUDA graph; roofline from "
+                               "per-stage events of plan + attend",
                          "parity": r["parity"], "gpu_launches": r["launches"]}
             if published is not None:
                 line[key]["published_ascend_us"] = published
