@@ -90,3 +90,29 @@ def test_two_gpu_sharded_call_matches_the_oracle(causal):
         visible = np.asarray(LENGTHS)[:, None] - (CASE["sq"] - 1 - np.arange(CASE["sq"]))[None] if causal \
             else np.repeat(np.asarray(LENGTHS)[:, None], CASE["sq"], 1)
         assert not by_head[visible <= 0].any() and not by_batch[visible <= 0].any()
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_device_list_call_from_one_process_matches_the_oracle(causal):
+    # mha_paged_decode_devices: the head partition driven from one process, one launch per GPU on its current
+    # stream, then the whole output assembled on GPU 0 by peer copies.
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    from fixtures import MAX_ABS
+    from oracle import paged_attention
+    from fgw_b200.operators.mha import sharded
+    q, k, v, table, lengths = _inputs()
+    shards = []
+    for rank in range(2):
+        dev = torch.device("cuda", rank)
+        first, count = sharded.head_shard(CASE["heads"], rank, 2)
+        h = slice(first, first + count)
+        shards.append((q[:, :, h].contiguous().to(dev), k[:, h].contiguous().to(dev), v[:, h].contiguous().to(dev),
+                       table.to(dev), lengths.to(dev)))
+    full = sharded.mha_paged_decode_devices(shards, CASE["page"], causal, gather_device="cuda:0")
+    torch.cuda.synchronize()
+    got = full.float().cpu().numpy()
+    want = paged_attention(q.float().numpy(), k.float().numpy(), v.float().numpy(), table.numpy(), lengths.numpy(),
+                           CASE["page"], causal)
+    assert got.shape == want.shape
+    assert np.abs(got - want).max() <= MAX_ABS["bfloat16"]
