@@ -120,6 +120,27 @@ def test_config2_long_query_whole_output(sq, kernel):
     _check_all(out, q, k, v, table, lengths.cpu(), page, False)
 
 
+@pytest.mark.parametrize("dtype,causal,dim,kernel", [
+    (torch.bfloat16, True, 128, "auto"), (torch.float16, False, 128, "auto"), (torch.bfloat16, False, 64, "auto"),
+    (torch.bfloat16, True, 64, "halves"), (torch.float16, True, 256, "auto")],
+    ids=["bf16_causal_d128", "fp16_d128", "bf16_d64", "bf16_causal_d64_halves", "fp16_causal_d256"])
+def test_config2_shape_variants_whole_output(dtype, causal, dim, kernel):
+    # Config 2's shape (B2 H8 Q4096 KV2048, page 128, shuffled table) with the other dtype, causal masking and the
+    # other head-dimension blocks (D64: one 64-column block per operand; D256: the one-tile kernel), whole output.
+    from fgw_b200.operators.mha.current import mha_paged_decode
+    batch, heads, page, kv, sq = 2, 8, 128, 2048, 4096
+    width = kv // page
+    table = torch.randperm(batch * width, generator=torch.Generator().manual_seed(77)).reshape(batch, width)
+    table = table.to(torch.int32).to(DEV)
+    gen = torch.Generator(device=DEV).manual_seed(77 + dim)
+    q = torch.randn(batch, sq, heads, dim, generator=gen, device=DEV).to(dtype)
+    k, v = _pool(batch * width * page, heads, dim, dtype, gen)
+    lengths = torch.tensor([kv, kv - 333], dtype=torch.int32, device=DEV)
+    kwargs = {} if kernel == "auto" else {"path": "tensor", "tensor_kernel": kernel}
+    out = mha_paged_decode(q, k, v, table, lengths, page, causal, **kwargs)
+    _check_all(out, q, k, v, table, lengths.cpu(), page, causal)
+
+
 CONFIG3 = [(b, h, sq, kv) for (b, h) in ((1, 1), (2, 8)) for sq in (1, 4, 16, 64, 512)
            for kv in (512, 2048, 8192, 32768)]
 
