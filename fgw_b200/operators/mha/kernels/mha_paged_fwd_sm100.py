@@ -19,6 +19,7 @@ Knobs of the Ascend pipeline (``pipeline_stages``, ``buffer_versions``, ``kv_ver
 callable; the CUDA kernels size their own TMA rings, so they do not change the schedule.
 ``persistent_programs`` caps the persistent grid (default: the SM count; ``None`` uncapped).
 """
+import collections
 import functools
 import threading
 
@@ -95,8 +96,38 @@ def _native_split_model():
 
 _route_cached = functools.lru_cache(maxsize=64)(route)
 
-_KEPT_WORKSPACE_BYTES = 64 << 20  # a launcher keeps workspaces up to this size between eager calls
-_KEPT_WORKSPACES = 8              # (device, stream) pairs per launcher
+_KEPT_WORKSPACE_BYTES = 64 << 20  # workspaces up to this size are kept between eager calls
+_KEPT_TOTAL_BYTES = 256 << 20     # all kept workspaces of the process together, least recently used dropped first
+
+
+class _KeptWorkspaces:
+    """Workspaces of eager launcher calls that pass none, kept per (launcher, device, stream) so that a serving loop
+    saves an allocation per call. Calls on one stream run in order, so the next call on that stream may reuse its
+    workspace (the plan launch re-initialises what the kernels read); a workspace is allocated on the stream it
+    serves, so dropping one is ordered after the work that used it. One lock covers the lookup and the enqueue
+    (ctypes releases the GIL during the call), so two threads never interleave their launches on one workspace."""
+
+    def __init__(self, cap):
+        self.cap = cap
+        self.bytes = 0
+        self.items = collections.OrderedDict()
+        self.lock = threading.Lock()
+
+    def get(self, key, nbytes, make):
+        """The kept workspace for ``key`` (made by ``make()`` on a miss); the caller holds ``lock``."""
+        ws = self.items.get(key)
+        if ws is not None:
+            self.items.move_to_end(key)
+            return ws
+        while self.items and self.bytes + nbytes > self.cap:
+            _, old = self.items.popitem(last=False)
+            self.bytes -= old.numel()
+        ws = self.items[key] = make()
+        self.bytes += ws.numel()
+        return ws
+
+
+_KEPT = _KeptWorkspaces(_KEPT_TOTAL_BYTES)
 
 
 def _current_stream(device):
@@ -290,13 +321,11 @@ def build_kernel(batch, sq, heads, dim, pool_rows, width, page_size, causal, dty
     def _workspace(device):
         return torch.empty(max(workspace_bytes, 256), dtype=torch.uint8, device=device)
 
-    # Workspaces of eager calls that pass none, kept per (device, stream): calls on one stream run in order, so
-    # the next call may reuse the workspace (the plan launch re-initialises what the kernels read), and a
-    # serving loop saves an allocation per call. A call being captured into a CUDA graph gets a workspace of its
-    # own (the graph keeps it), and large workspaces (many splits) are not kept.
-    kept = {}
-    kept_lock = threading.Lock()
+    # Eager calls that pass no workspace reuse one kept for this launcher, device and stream (_KeptWorkspaces);
+    # a call being captured into a CUDA graph gets a workspace of its own (the graph keeps it), and large
+    # workspaces (many splits) are not kept.
     keep = workspace_bytes <= _KEPT_WORKSPACE_BYTES
+    launcher_id = object()
 
     def launch(q, k, v, table, lengths, out=None, workspace=None):
         out = torch.empty_like(q) if out is None else out
@@ -306,12 +335,8 @@ def build_kernel(batch, sq, heads, dim, pool_rows, width, page_size, causal, dty
             ws = _workspace(q.device) if workspace is None else workspace
             _native.paged_fwd(_bind(q, k, v, table, lengths, out), ws.data_ptr(), ws.numel(), stream)
             return out
-        with kept_lock:  # one enqueue at a time per kept workspace (ctypes releases the GIL in the call)
-            ws = kept.get((device, stream))
-            if ws is None:
-                if len(kept) >= _KEPT_WORKSPACES:
-                    kept.clear()
-                ws = kept[(device, stream)] = _workspace(q.device)
+        with _KEPT.lock:
+            ws = _KEPT.get((launcher_id, device, stream), max(workspace_bytes, 256), lambda: _workspace(q.device))
             _native.paged_fwd(_bind(q, k, v, table, lengths, out), ws.data_ptr(), ws.numel(), stream)
         return out
 

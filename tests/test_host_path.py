@@ -1,4 +1,5 @@
-"""The library's host split choice (fgw_mha_choose_splits) against the Python restatement of the B200 model.
+"""The host side of a call: the library's split choice (fgw_mha_choose_splits) against the Python restatement of
+the B200 model, and the workspaces kept between eager launcher calls.
 
 The serving path hands the host copy of its cache lengths to the library, which range-checks them and picks the
 split count in one pass (no CUDA call, so this runs on CPU). It must pick exactly what
@@ -89,3 +90,26 @@ def test_binding_takes_only_the_batch_int32_lengths():
                 np.array([5, 0, 6, 0], dtype=np.int32)[::2]):
         with pytest.raises(ValueError):
             _native.choose_splits(model, bad, 2, 1, 8, 128, 64, 10, 148)
+
+
+def test_kept_workspaces_stay_under_their_byte_cap_least_recently_used_first():
+    # Eager launcher calls without a workspace reuse one kept per (launcher, device, stream); the process-wide pool
+    # drops the least recently used workspace once the total would pass its cap.
+    from fgw_b200.operators.mha.kernels.mha_paged_fwd_sm100 import _KeptWorkspaces
+
+    class Buffer:
+        def __init__(self, nbytes):
+            self.nbytes = nbytes
+
+        def numel(self):
+            return self.nbytes
+
+    pool = _KeptWorkspaces(100)
+    with pool.lock:
+        a = pool.get(("x", 0, 1), 40, lambda: Buffer(40))
+        pool.get(("y", 0, 1), 40, lambda: Buffer(40))
+        assert pool.get(("x", 0, 1), 40, lambda: Buffer(40)) is a  # a hit; x is now the most recent
+        pool.get(("z", 0, 1), 40, lambda: Buffer(40))             # drops y
+        assert set(pool.items) == {("x", 0, 1), ("z", 0, 1)} and pool.bytes == 80
+        pool.get(("w", 0, 2), 90, lambda: Buffer(90))             # drops both
+        assert set(pool.items) == {("w", 0, 2)} and pool.bytes == 90
