@@ -367,12 +367,19 @@ __global__ void __launch_bounds__(384, 1)
         umma_commit(&s_full[t]);
       };
       // O_t += P_t V: P_t read from TMEM (packed into the first 64 columns of S_t), V from stage `st`.
+      // The P column and V descriptor advance by one step per MMA through opaque registers: with all eight
+      // operand pairs formed up front the issuer needs more than the control warpgroup's registers and
+      // spills, and the reloads sit between the MMA issues.
       auto pv = [&](int t, int st, bool first) {
-        const uint32_t b_lo = v_lo + static_cast<uint32_t>((st * S::kKVBytes) >> 4);
+        uint32_t b_lo = v_lo + static_cast<uint32_t>((st * S::kKVBytes) >> 4);
+        uint32_t p_col = tmem + S::s_col(t);
+        const uint32_t o_tmem = tmem + S::o_col(t);
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
-          umma_f16_ts_w(tmem + S::o_col(t), tmem + S::s_col(t) + kk * 8, b_lo + ((kk * 16 * 128) >> 4), kHi, idesc_pv,
-                        (!first || kk > 0) ? 1u : 0u);
+          umma_f16_ts_w(o_tmem, p_col, b_lo, kHi, idesc_pv, (!first || kk > 0) ? 1u : 0u);
+          p_col += 8;
+          b_lo += (16 * 128) >> 4;
+          asm volatile("" : "+r"(p_col), "+r"(b_lo));
         }
       };
       SegmentCursor cur;
