@@ -5,8 +5,8 @@
 // What changes is the schedule:
 //   * a work item is a pair of 128-row query tiles (A, B) of one (request, head, split); both share every
 //     K/V tile, so K/V shared-memory traffic per FLOP halves;
-//   * two softmax warpgroups (warps 4-7 for A, 8-11 for B) ping-pong on the tensor core. The single MMA
-//     thread issues, per KV tile j:  PV_A(j), QK_A(j+1), PV_B(j), QK_B(j+1)  so the softmax of A(j+1)
+//   * two softmax warpgroups (warps 4-7 for A, 8-11 for B) ping-pong on the tensor core. The MMA warp
+//     issues, per KV tile j:  PV_A(j), QK_A(j+1), PV_B(j), QK_B(j+1)  so the softmax of A(j+1)
 //     overlaps PV_B(j) + QK_B(j+1) and the softmax of B(j) overlaps PV_A(j) + QK_A(j+1);
 //   * P never touches shared memory: each softmax thread writes its bf16/fp16 P row back into the TMEM
 //     columns of the S row it has just consumed, and PV reads P straight from TMEM (tcgen05.mma with the
@@ -73,6 +73,13 @@ struct Fmha2Shape {
   static constexpr int kTmemSlot = kBar + kNumBars * 8;
   static constexpr int kBytes = kTmemSlot + 16 + 1024;
 };
+
+// max(a, b, c) in one instruction (sm_100 three-input max; NaN-free inputs here)
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
 
 struct PairItem {
   int b, h, s, q0, len, n_begin, n, n_tile[2];
@@ -324,10 +331,15 @@ __global__ void __launch_bounds__(384, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------------- UMMA issuer
-    if (lane == 0) {
+    // The whole warp runs this role converged, with its loop state kept warp-uniform (segment fields are
+    // broadcast from lane 0), and every tcgen05 issue is predicated on one elected lane. Against a lone lane 0
+    // running the same code this measured 105.4 against 111.6 us on config 2 (619 against 654 us at Q = 32768).
+    {
+      const uint32_t leader = elect_one_sync();
+      const uint32_t tmem_u = __shfl_sync(0xffffffffu, tmem, 0);
       bool ok = true;
       uint32_t kc = 0, vc = 0, qc = 0;
-      uint32_t pc[2] = {0, 0}, oc[2] = {0, 0};
+      uint32_t pbits = 0, obits = 0;  // bit t: phase parity of p_full[t] / o_empty[t] uses
       const int fmt = Tr::kUmmaFormat;
       const uint32_t idesc_qk = umma_idesc_f16(fmt, 128, BN, 0, 0);
       const uint32_t idesc_pv = umma_idesc_f16(fmt, 128, D, 0, 1);
@@ -338,18 +350,18 @@ __global__ void __launch_bounds__(384, 1)
       constexpr uint32_t kHi = umma_desc_hi(1024, 2);
       const int ksteps_qk = D / 16;
       auto wait_or_fail = [&](uint64_t* bar, uint32_t parity, int site) {
-        if (ok && !mbar_wait(bar, parity, a.budget_ns)) {
+        if (ok && !__all_sync(0xffffffffu, mbar_wait(bar, parity, a.budget_ns))) {
           ok = false;
-          record_error(a.ws, FGW_ERR_DEVICE_TIMEOUT, site);
+          if (lane == 0) record_error(a.ws, FGW_ERR_DEVICE_TIMEOUT, site);
         }
         return ok;
       };
       // Several phases at once (null entries are skipped): one polling loop instead of a chain of waits.
       auto wait_all_or_fail = [&](uint64_t* b0, uint32_t p0, uint64_t* b1, uint32_t p1, uint64_t* b2, uint32_t p2,
                                   uint64_t* b3, uint32_t p3, int site) {
-        if (ok && !mbar_wait_all(b0, p0, b1, p1, b2, p2, b3, p3, a.budget_ns)) {
+        if (ok && !__all_sync(0xffffffffu, mbar_wait_all(b0, p0, b1, p1, b2, p2, b3, p3, a.budget_ns))) {
           ok = false;
-          record_error(a.ws, FGW_ERR_DEVICE_TIMEOUT, site);
+          if (lane == 0) record_error(a.ws, FGW_ERR_DEVICE_TIMEOUT, site);
         }
         return ok;
       };
@@ -360,11 +372,11 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll
         for (int kk = 0; kk < 4 * NB; ++kk) {
           if (kk < ksteps_qk) {
-            umma_f16_ss_w(tmem + S::s_col(t), a_lo + (((kk >> 2) * S::kTileBytes + (kk & 3) * 32) >> 4), kHi,
+            umma_f16_ss_e(leader, tmem_u + S::s_col(t), a_lo + (((kk >> 2) * S::kTileBytes + (kk & 3) * 32) >> 4), kHi,
                           b_lo + (((kk >> 2) * BN * 128 + (kk & 3) * 32) >> 4), kHi, idesc_qk, kk > 0 ? 1u : 0u);
           }
         }
-        umma_commit(&s_full[t]);
+        umma_commit_e(leader, &s_full[t]);
       };
       // O_t += P_t V: P_t read from TMEM (packed into the first 64 columns of S_t), V from stage `st`.
       // The P column and V descriptor advance by one step per MMA through opaque registers: with all eight
@@ -372,11 +384,11 @@ __global__ void __launch_bounds__(384, 1)
       // spills, and the reloads sit between the MMA issues.
       auto pv = [&](int t, int st, bool first) {
         uint32_t b_lo = v_lo + static_cast<uint32_t>((st * S::kKVBytes) >> 4);
-        uint32_t p_col = tmem + S::s_col(t);
-        const uint32_t o_tmem = tmem + S::o_col(t);
+        uint32_t p_col = tmem_u + S::s_col(t);
+        const uint32_t o_tmem = tmem_u + S::o_col(t);
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
-          umma_f16_ts_w(o_tmem, p_col, b_lo, kHi, idesc_pv, (!first || kk > 0) ? 1u : 0u);
+          umma_f16_ts_e(leader, o_tmem, p_col, b_lo, kHi, idesc_pv, (!first || kk > 0) ? 1u : 0u);
           p_col += 8;
           b_lo += (16 * 128) >> 4;
           asm volatile("" : "+r"(p_col), "+r"(b_lo));
@@ -385,8 +397,11 @@ __global__ void __launch_bounds__(384, 1)
       SegmentCursor cur;
       cursor_init(a, cur);
       Segment sg;
-      while (next_segment(a, cur, sg)) {
-        const PairItem& c = sg.c;
+      while (__shfl_sync(0xffffffffu, static_cast<int>(next_segment(a, cur, sg)), 0)) {
+        PairItem c = sg.c;  // the fields this role branches on, made warp-uniform
+        c.n = __shfl_sync(0xffffffffu, c.n, 0);
+        c.n_tile[0] = __shfl_sync(0xffffffffu, c.n_tile[0], 0);
+        c.n_tile[1] = __shfl_sync(0xffffffffu, c.n_tile[1], 0);
         if (c.n <= 0) continue;
         // prologue: S_A(0), S_B(0) once Q and K(0) are in
         int kst = kc % NS;
@@ -395,11 +410,11 @@ __global__ void __launch_bounds__(384, 1)
           for (int t = 0; t < 2; ++t) {
             if (c.n_tile[t] > 0) qk(t, kst);
           }
-          umma_commit(&k_empty[kst]);
+          umma_commit_e(leader, &k_empty[kst]);
         }
         ++qc;
         ++kc;
-        if (c.n == 1 && ok) umma_commit(q_empty);
+        if (c.n == 1 && ok) umma_commit_e(leader, q_empty);
         for (int j = 0; j < c.n; ++j) {
           // Opaque to the compiler, so the descriptor sums are formed where they are used instead of being
           // hoisted out of the loops (which would keep one register per stage and step live).
@@ -411,42 +426,43 @@ __global__ void __launch_bounds__(384, 1)
           const int knext = kc % NS;
           const uint32_t k_par = (kc / NS) & 1;
           bool v_seen = false, k_seen = !more;
+#pragma unroll 1
           for (int t = 0; t < 2; ++t) {
-            const bool pv_t = j < c.n_tile[t];
-            const bool qk_t = more && j + 1 < c.n_tile[t];
+            const int nt = t ? c.n_tile[1] : c.n_tile[0];
+            const bool pv_t = j < nt;
+            const bool qk_t = more && j + 1 < nt;
             if (pv_t || qk_t) {
               // this tile's P, the V tile, the next K tile and (first tile of an item) an empty O, in one poll
-              const bool ready = wait_all_or_fail(pv_t ? &p_full[t] : nullptr, pc[t] & 1,
+              const bool ready = wait_all_or_fail(pv_t ? &p_full[t] : nullptr, (pbits >> t) & 1,
                                                   (pv_t && !v_seen) ? &v_full[vst] : nullptr, v_par,
                                                   (qk_t && !k_seen) ? &k_full[knext] : nullptr, k_par,
-                                                  (pv_t && j == 0) ? &o_empty[t] : nullptr, (oc[t] & 1) ^ 1, 53 + t);
+                                                  (pv_t && j == 0) ? &o_empty[t] : nullptr, ((obits >> t) & 1) ^ 1, 53 + t);
               v_seen = v_seen || pv_t;
               k_seen = k_seen || qk_t;
               if (ready) {
                 tc_fence_after_sync();
                 if (pv_t) {
                   pv(t, vst, j == 0);
-                  if (j + 1 == c.n_tile[t]) umma_commit(&pv_done[t]);
+                  if (j + 1 == nt) umma_commit_e(leader, &pv_done[t]);
                 }
                 if (qk_t) qk(t, knext);
               }
             }
-            if (pv_t) ++pc[t];
+            if (pv_t) pbits ^= 1u << t;
           }
-          if (ok) umma_commit(&v_empty[vst]);
+          if (ok) umma_commit_e(leader, &v_empty[vst]);
           if (more) {
-            if (ok) umma_commit(&k_empty[knext]);
+            if (ok) umma_commit_e(leader, &k_empty[knext]);
             ++kc;
-            if (j + 2 == c.n && ok) umma_commit(q_empty);  // every QK of this item is now issued
+            if (j + 2 == c.n && ok) umma_commit_e(leader, q_empty);  // every QK of this item is now issued
           }
         }
-        for (int t = 0; t < 2; ++t) {
-          if (c.n_tile[t] > 0) ++oc[t];
-        }
+        if (c.n_tile[0] > 0) obits ^= 1u;
+        if (c.n_tile[1] > 0) obits ^= 2u;
       }
       if (ok) {
-        umma_commit(mma_done);
-        mbar_wait(mma_done, 0, a.budget_ns);
+        umma_commit_e(leader, mma_done);
+        __all_sync(0xffffffffu, mbar_wait(mma_done, 0, a.budget_ns));
       }
     }
   } else if (warp >= 4) {
@@ -506,11 +522,16 @@ __global__ void __launch_bounds__(384, 1)
           }
         }
         auto sval = [&](int col) -> float { return __uint_as_float(sr[col]); };
-        float mx_raw = -INFINITY;
+        // four independent chains of three-input maxima (two new scores per instruction)
+        float mq0 = -INFINITY, mq1 = -INFINITY, mq2 = -INFINITY, mq3 = -INFINITY;
 #pragma unroll
-        for (int col = 0; col < BN; col += 4) {
-          mx_raw = fmaxf(mx_raw, fmaxf(fmaxf(sval(col), sval(col + 1)), fmaxf(sval(col + 2), sval(col + 3))));
+        for (int col = 0; col < BN; col += 8) {
+          mq0 = fmax3(mq0, sval(col), sval(col + 1));
+          mq1 = fmax3(mq1, sval(col + 2), sval(col + 3));
+          mq2 = fmax3(mq2, sval(col + 4), sval(col + 5));
+          mq3 = fmax3(mq3, sval(col + 6), sval(col + 7));
         }
+        const float mx_raw = fmax3(mq0, mq1, fmaxf(mq2, mq3));
         const float mx = mx_raw * a.scale_log2;  // scale > 0; -inf stays -inf
         float m_new = m;
         bool grow = false;
@@ -549,7 +570,10 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll
           for (int half = 0; half < 2; ++half) {
             uint32_t packed[32];
-            if (tail) {
+            // One inlined copy of the exponential loop when every pair goes to the SFU: the per-tile code of
+            // the softmax, MMA and TMA warps shares the SM's instruction caches, and the duplicate copy measured
+            // ~2 % slower (111.6 against 113.7 us on config 2).
+            if (S::kFmaEvery == 0 || tail) {
               exp2_pack_half<Tr, 0>(&sr[half * 64], scale2, negm2, acc, packed);
             } else {
               exp2_pack_half<Tr, S::kFmaEvery>(&sr[half * 64], scale2, negm2, acc, packed);
