@@ -375,10 +375,18 @@ __global__ void __launch_bounds__(384, 1)
         }
         return ok;
       };
-      // Several phases at once (null entries are skipped): one polling loop instead of a chain of waits.
+      // Several phases (null entries are skipped), waited for in turn with try_wait, which suspends the warp
+      // until the phase completes or a hardware time limit passes: the buffers first, the tile's P (b0), the one
+      // usually still pending, last. With the converged warp this measured 97.3 against 101.4 us on config 2
+      // (578 against 611 us at Q = 32768) over polling all four with test_wait in one loop.
       auto wait_all_or_fail = [&](uint64_t* b0, uint32_t p0, uint64_t* b1, uint32_t p1, uint64_t* b2, uint32_t p2,
                                   uint64_t* b3, uint32_t p3, int site) {
-        if (ok && !__all_sync(0xffffffffu, mbar_wait_all(b0, p0, b1, p1, b2, p2, b3, p3, a.budget_ns))) {
+        if (!ok) return false;
+        const bool got = (b1 == nullptr || mbar_wait(b1, p1, a.budget_ns)) &&
+                         (b2 == nullptr || mbar_wait(b2, p2, a.budget_ns)) &&
+                         (b3 == nullptr || mbar_wait(b3, p3, a.budget_ns)) &&
+                         (b0 == nullptr || mbar_wait(b0, p0, a.budget_ns));
+        if (!__all_sync(0xffffffffu, got)) {
           ok = false;
           if (lane == 0) record_error(a.ws, FGW_ERR_DEVICE_TIMEOUT, site);
         }
