@@ -156,82 +156,87 @@ __global__ void __launch_bounds__(256, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------------------- TMA producer
-    if (lane == 0) {
-      tma_prefetch_desc(&qmap);
-      tma_prefetch_desc(&kmap);
-      tma_prefetch_desc(&vmap);
+    // Converged warp, lane 0 issues; the item's block-table entries are read 32 pages at a time (one per lane)
+    // ahead of the waits and broadcast per box (as in the two-tile kernel, fgw_fmha2_sm100.cu).
+    {
+      if (lane == 0) {
+        tma_prefetch_desc(&qmap);
+        tma_prefetch_desc(&kmap);
+        tma_prefetch_desc(&vmap);
+      }
       bool ok = true;
       uint32_t kc = 0, vc = 0, qc = 0;
       const int boxes = BN / a.box_rows;
       const uint32_t box_bytes = a.box_rows * 128;
+      auto wait_or_fail = [&](uint64_t* bar, uint32_t parity, int site) {
+        if (ok && !__all_sync(0xffffffffu, mbar_wait(bar, parity, a.budget_ns))) {
+          ok = false;
+          if (lane == 0) record_error(a.ws, FGW_ERR_DEVICE_TIMEOUT, site);
+        }
+        return ok;
+      };
       for (long long item = blockIdx.x; item < a.items; item += grid) {
         ItemCoords c;
         tensor_item(a, item, BN, c);
+        c.n_begin = __shfl_sync(0xffffffffu, c.n_begin, 0);
+        c.n_end = __shfl_sync(0xffffffffu, c.n_end, 0);
         if (c.n_end <= c.n_begin) continue;
+        const int32_t* row_table = a.table + (long long)c.b * a.width;
+        int chunk = ((c.n_begin * BN) / a.page) & ~31;
+        int entry = (chunk + lane < a.width) ? row_table[chunk + lane] : 0;
         // Q tile: wait until the previous item's last QK has read it.
-        if (ok && !mbar_wait(q_empty, (qc & 1) ^ 1, a.budget_ns)) {
-          ok = false;
-          record_error(a.ws, FGW_ERR_DEVICE_TIMEOUT, 10);
-        }
-        if (ok) {
+        if (wait_or_fail(q_empty, (qc & 1) ^ 1, 10) && lane == 0) {
           mbar_arrive_expect_tx(q_full, NB * S::kBlockBytes);
           for (int blk = 0; blk < NB; ++blk) {
             tma_load_4d(q_smem + blk * S::kBlockBytes, &qmap, q_full, blk * 64, c.h, c.q0, c.b);
           }
         }
         ++qc;
-        const int32_t* row_table = a.table + (long long)c.b * a.width;
         const int end_tok = c.len;
         for (int j = c.n_begin; j < c.n_end; ++j) {
           const int tok0 = j * BN;
           int nbox = 0;
           for (int k = 0; k < boxes; ++k) nbox += (tok0 + k * a.box_rows < end_tok) ? 1 : 0;
-          // K tile
-          {
-            const int st = kc % NS;
-            if (ok && !mbar_wait(&k_empty[st], ((kc / NS) & 1) ^ 1, a.budget_ns)) {
-              ok = false;
-              record_error(a.ws, FGW_ERR_DEVICE_TIMEOUT, 11);
-            }
-            if (ok) {
-              mbar_arrive_expect_tx(&k_full[st], NB * nbox * box_bytes);
-              uint8_t* dst = k_smem + st * S::kKVBytes;
+          // K tile, then V tile
+#pragma unroll
+          for (int which = 0; which < 2; ++which) {
+            const uint32_t cnt = which == 0 ? kc : vc;
+            uint64_t* full = which == 0 ? k_full : v_full;
+            uint64_t* empty = which == 0 ? k_empty : v_empty;
+            const CUtensorMap* map = which == 0 ? &kmap : &vmap;
+            uint8_t* ring = which == 0 ? k_smem : v_smem;
+            const int st = cnt % NS;
+            if (wait_or_fail(&empty[st], ((cnt / NS) & 1) ^ 1, 11 + which)) {
+              if (lane == 0) mbar_arrive_expect_tx(&full[st], NB * nbox * box_bytes);
+              uint8_t* dst = ring + st * S::kKVBytes;
               for (int k = 0; k < nbox; ++k) {
                 const int tok = tok0 + k * a.box_rows;
-                const int row = row_table[tok / a.page] * a.page + tok % a.page;
-                for (int blk = 0; blk < NB; ++blk) {
-                  tma_load_3d(dst + blk * BN * 128 + k * box_bytes, &kmap, &k_full[st], blk * 64, c.h, row);
+                const int pg = tok / a.page;  // < width: only boxes before the cache end are loaded
+                if ((pg & ~31) != chunk) {
+                  chunk = pg & ~31;
+                  entry = (chunk + lane < a.width) ? row_table[chunk + lane] : 0;
+                }
+                const int row = __shfl_sync(0xffffffffu, entry, pg & 31) * a.page + tok % a.page;
+                if (lane == 0) {
+                  for (int blk = 0; blk < NB; ++blk) {
+                    tma_load_3d(dst + blk * BN * 128 + k * box_bytes, map, &full[st], blk * 64, c.h, row);
+                  }
                 }
               }
             }
-            ++kc;
           }
-          // V tile
-          {
-            const int st = vc % NS;
-            if (ok && !mbar_wait(&v_empty[st], ((vc / NS) & 1) ^ 1, a.budget_ns)) {
-              ok = false;
-              record_error(a.ws, FGW_ERR_DEVICE_TIMEOUT, 12);
-            }
-            if (ok) {
-              mbar_arrive_expect_tx(&v_full[st], NB * nbox * box_bytes);
-              uint8_t* dst = v_smem + st * S::kKVBytes;
-              for (int k = 0; k < nbox; ++k) {
-                const int tok = tok0 + k * a.box_rows;
-                const int row = row_table[tok / a.page] * a.page + tok % a.page;
-                for (int blk = 0; blk < NB; ++blk) {
-                  tma_load_3d(dst + blk * BN * 128 + k * box_bytes, &vmap, &v_full[st], blk * 64, c.h, row);
-                }
-              }
-            }
-            ++vc;
-          }
+          ++kc;
+          ++vc;
         }
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------------- UMMA issuer
-    if (lane == 0) {
+    // Converged warp with warp-uniform loop state; every tcgen05 issue is predicated on one elected lane, and
+    // the waits are try_wait (as in the two-tile kernel).
+    {
+      const uint32_t leader = elect_one_sync();
+      const uint32_t tmem_u = __shfl_sync(0xffffffffu, tmem, 0);
       bool ok = true;
       uint32_t kc = 0, vc = 0, qc = 0, sc = 0, pc = 0, oc = 0;
       const int fmt = Tr::kUmmaFormat;
@@ -245,9 +250,9 @@ __global__ void __launch_bounds__(256, 1)
       const int ksteps_pv = BN / 16;
 
       auto wait_or_fail = [&](uint64_t* bar, uint32_t parity, int site) {
-        if (ok && !mbar_wait(bar, parity, a.budget_ns)) {
+        if (ok && !__all_sync(0xffffffffu, mbar_wait(bar, parity, a.budget_ns))) {
           ok = false;
-          record_error(a.ws, FGW_ERR_DEVICE_TIMEOUT, site);
+          if (lane == 0) record_error(a.ws, FGW_ERR_DEVICE_TIMEOUT, site);
         }
         return ok;
       };
@@ -260,28 +265,32 @@ __global__ void __launch_bounds__(256, 1)
             const uint32_t off = (kk & 3) * 32;  // 16 elements further along the 128-byte swizzled row
             const uint64_t adesc = umma_smem_desc(q_base + (kk >> 2) * S::kBlockBytes + off, 16, 1024, 2);
             const uint64_t bdesc = umma_smem_desc(kst + (kk >> 2) * BN * 128 + off, 16, 1024, 2);
-            umma_f16_ss(tmem + s_buf * S::kSCols, adesc, bdesc, idesc_qk, kk > 0 ? 1u : 0u);
+            umma_f16_ss_e(leader, tmem_u + s_buf * S::kSCols, static_cast<uint32_t>(adesc),
+                          static_cast<uint32_t>(adesc >> 32), static_cast<uint32_t>(bdesc),
+                          static_cast<uint32_t>(bdesc >> 32), idesc_qk, kk > 0 ? 1u : 0u);
           }
-          umma_commit(&k_empty[st]);
-          umma_commit(&s_full[s_buf]);
+          umma_commit_e(leader, &k_empty[st]);
+          umma_commit_e(leader, &s_full[s_buf]);
         }
         ++kc;
       };
       auto issue_pv = [&](bool first) {
         const int st = vc % NS;
-        bool ready = wait_or_fail(p_full, pc & 1, 22);
-        ready = ready && wait_or_fail(&v_full[st], (vc / NS) & 1, 23);
+        bool ready = wait_or_fail(&v_full[st], (vc / NS) & 1, 23);
         if (first) ready = ready && wait_or_fail(o_empty, (oc & 1) ^ 1, 24);
+        ready = ready && wait_or_fail(p_full, pc & 1, 22);
         if (ready) {
           tc_fence_after_sync();
           const uint32_t vst = v_base + st * S::kKVBytes;
           for (int kk = 0; kk < ksteps_pv; ++kk) {
             const uint64_t adesc = umma_smem_desc(p_base + (kk >> 2) * S::kBlockBytes + (kk & 3) * 32, 16, 1024, 2);
             const uint64_t bdesc = umma_smem_desc(vst + kk * 16 * 128, BN * 128, 1024, 2);
-            umma_f16_ss(tmem + S::kOCol, adesc, bdesc, idesc_pv, (!first || kk > 0) ? 1u : 0u);
+            umma_f16_ss_e(leader, tmem_u + S::kOCol, static_cast<uint32_t>(adesc), static_cast<uint32_t>(adesc >> 32),
+                          static_cast<uint32_t>(bdesc), static_cast<uint32_t>(bdesc >> 32), idesc_pv,
+                          (!first || kk > 0) ? 1u : 0u);
           }
-          umma_commit(&v_empty[st]);
-          umma_commit(pv_done);
+          umma_commit_e(leader, &v_empty[st]);
+          umma_commit_e(leader, pv_done);
         }
         ++vc;
         ++pc;
@@ -290,7 +299,7 @@ __global__ void __launch_bounds__(256, 1)
       for (long long item = blockIdx.x; item < a.items; item += grid) {
         ItemCoords c;
         tensor_item(a, item, BN, c);
-        const int n = c.n_end - c.n_begin;
+        const int n = __shfl_sync(0xffffffffu, c.n_end - c.n_begin, 0);
         if (n <= 0) continue;
         const bool have_q = wait_or_fail(q_full, qc & 1, 20);
         (void)have_q;
@@ -301,7 +310,7 @@ __global__ void __launch_bounds__(256, 1)
             issue_qk(sc & 1);
             ++sc;
           }
-          if (j + 1 == n && ok) umma_commit(q_empty);  // every QK of this item has been issued
+          if (j + 1 == n && ok) umma_commit_e(leader, q_empty);  // every QK of this item has been issued
           issue_pv(j == 0);
         }
         ++qc;
@@ -309,8 +318,8 @@ __global__ void __launch_bounds__(256, 1)
       }
       // Drain: make sure every UMMA issued above has completed before TMEM is released.
       if (ok) {
-        umma_commit(mma_done);
-        mbar_wait(mma_done, 0, a.budget_ns);
+        umma_commit_e(leader, mma_done);
+        __all_sync(0xffffffffu, mbar_wait(mma_done, 0, a.budget_ns));
       }
     }
   } else if (warp >= 4) {
