@@ -207,6 +207,12 @@ struct ElemTraits<__nv_bfloat16> {
     return *reinterpret_cast<uint32_t*>(&v);
   }
   __device__ __forceinline__ static __nv_bfloat16 from_float(float x) { return __float2bfloat16_rn(x); }
+  // acc + the two packed values, each added in FP32 (sm_100 mixed-precision add)
+  __device__ __forceinline__ static float2 add2(float2 acc, uint32_t bits) {
+    asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\tadd.rn.f32.bf16 %0, lo, %0;\n\t"
+        "add.rn.f32.bf16 %1, hi, %1;\n\t}" : "+f"(acc.x), "+f"(acc.y) : "r"(bits));
+    return acc;
+  }
 };
 
 template <>
@@ -221,6 +227,11 @@ struct ElemTraits<__half> {
     return *reinterpret_cast<uint32_t*>(&v);
   }
   __device__ __forceinline__ static __half from_float(float x) { return __float2half_rn(x); }
+  __device__ __forceinline__ static float2 add2(float2 acc, uint32_t bits) {
+    asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\tadd.rn.f32.f16 %0, lo, %0;\n\t"
+        "add.rn.f32.f16 %1, hi, %1;\n\t}" : "+f"(acc.x), "+f"(acc.y) : "r"(bits));
+    return acc;
+  }
 };
 
 // 2^x through the SFU's approximate base-2 exponential (ex2.approx, flush-to-zero):

@@ -218,7 +218,7 @@ __device__ __forceinline__ void halves_exp2_pack(const uint32_t (&sr)[64], float
     packed[i] = Tr::pack2(fast_exp2(x.x), fast_exp2(x.y));
     // the row sum adds the rounded values PV multiplies (with the lazily rescaled running max a row's largest P
     // may exceed 1 and round; normalising by the unrounded sum would leave that rounding in the output)
-    acc[i % 4] = __fadd2_rn(acc[i % 4], Tr::unpack2(packed[i]));
+    acc[i % 4] = Tr::add2(acc[i % 4], packed[i]);
   }
 }
 

@@ -394,15 +394,17 @@ __global__ void __launch_bounds__(256, 1)
           alpha = (m == -INFINITY) ? 0.f : fast_exp2(m - m_new);
         }
         const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-        float rowsum = 0.f;
         uint32_t packed[BN / 2];
+        // four independent partial sums of pairs keep the add chain short
+        float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
         for (int i = 0; i < BN / 2; ++i) {
           packed[i] = Tr::pack2(fast_exp2(s[2 * i] - m_use), fast_exp2(s[2 * i + 1] - m_use));
           // the row sum adds the rounded values PV multiplies (the lazily rescaled max lets P exceed 1 and round)
-          const float2 r = Tr::unpack2(packed[i]);
-          rowsum += r.x + r.y;
+          acc[i % 4] = Tr::add2(acc[i % 4], packed[i]);
         }
+        const float rowsum =
+            (acc[0].x + acc[0].y) + (acc[1].x + acc[1].y) + (acc[2].x + acc[2].y) + (acc[3].x + acc[3].y);
         // PV of the previous tile must be finished before P is overwritten and O is rescaled.
         if (j > 0) wait_warp(pv_done, (pc - 1) & 1, 31);
         if (ok && warp_grow && j > 0) {
