@@ -100,45 +100,6 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64
   }
 }
 
-// Non-blocking test of one phase.
-__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
-  uint32_t done;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}\n"
-      : "=r"(done)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return done != 0;
-}
-
-// Waits until every listed phase has completed (a null barrier counts as complete). Each round tests all
-// pending barriers back to back, so the round trips of independent barriers overlap instead of adding up
-// (a single mbarrier test costs on the order of a couple of hundred cycles). Returns false if the budget
-// ran out first.
-__device__ __forceinline__ bool mbar_wait_all(uint64_t* b0, uint32_t p0, uint64_t* b1, uint32_t p1, uint64_t* b2,
-                                              uint32_t p2, uint64_t* b3, uint32_t p3, uint64_t budget_ns) {
-  bool d0 = b0 == nullptr, d1 = b1 == nullptr, d2 = b2 == nullptr, d3 = b3 == nullptr;
-  uint64_t start = 0;
-  for (uint32_t round = 0;; ++round) {
-    if (!d0) d0 = mbar_test_wait(b0, p0);
-    if (!d1) d1 = mbar_test_wait(b1, p1);
-    if (!d2) d2 = mbar_test_wait(b2, p2);
-    if (!d3) d3 = mbar_test_wait(b3, p3);
-    if (d0 && d1 && d2 && d3) return true;
-    // the clock is read only once the wait has lasted a while (reading it costs hundreds of cycles)
-    if ((round & 31) == 31) {
-      const uint64_t now = global_timer_ns();
-      if (round == 31) {
-        start = now;
-      } else if (now - start > budget_ns) {
-        return false;
-      }
-    }
-  }
-}
-
 // Named barrier over a subset of warps (id 0 is __syncthreads). These are the aligned forms: every lane of a
 // warp executes them together, so callers reconverge the warp (__syncwarp) first.
 __device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t threads) {
