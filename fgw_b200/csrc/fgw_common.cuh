@@ -100,6 +100,27 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64
   }
 }
 
+// One request's block-table row as seen by a converged warp: the entries of a 32-page window, one per lane, read
+// ahead of use and broadcast per lookup, so a producer's table reads leave its per-box path. Every lane must call
+// both members with the same arguments; page() re-reads the window only when the page leaves it.
+struct TableWindow {
+  const int32_t* row;
+  int width, base, entry;
+  __device__ __forceinline__ void init(const int32_t* row_, int width_, int first_page, int lane) {
+    row = row_;
+    width = width_;
+    base = first_page & ~31;
+    entry = (base + lane < width) ? row[base + lane] : 0;
+  }
+  __device__ __forceinline__ int page(int pg, int lane) {
+    if ((pg & ~31) != base) {
+      base = pg & ~31;
+      entry = (base + lane < width) ? row[base + lane] : 0;
+    }
+    return __shfl_sync(0xffffffffu, entry, pg & 31);
+  }
+};
+
 // Named barrier over a subset of warps (id 0 is __syncthreads). These are the aligned forms: every lane of a
 // warp executes them together, so callers reconverge the warp (__syncwarp) first.
 __device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t threads) {

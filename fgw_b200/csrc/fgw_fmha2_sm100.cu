@@ -303,9 +303,8 @@ __global__ void __launch_bounds__(384, 1)
         c.n_tile[1] = __shfl_sync(0xffffffffu, c.n_tile[1], 0);
         if (c.n <= 0) continue;
         const int32_t* row_table = a.table + (long long)c.b * a.width;
-        // this lane's entry of the 32-page chunk of the table that starts at page `chunk`
-        int chunk = ((c.n_begin * BN) / a.page) & ~31;
-        int entry = (chunk + lane < a.width) ? row_table[chunk + lane] : 0;
+        TableWindow table;
+        table.init(row_table, a.width, (c.n_begin * BN) / a.page, lane);
         if (wait_or_fail(q_empty, (qc & 1) ^ 1, 40) && lane == 0) {
           const int tiles_q = c.n_tile[1] > 0 ? 2 : 1;
           mbar_arrive_expect_tx(q_full, tiles_q * S::kQBytes);
@@ -336,11 +335,7 @@ __global__ void __launch_bounds__(384, 1)
               for (int k = 0; k < nbox; ++k) {
                 const int tok = tok0 + k * a.box_rows;
                 const int pg = tok / a.page;  // < width: only boxes before the cache end are loaded
-                if ((pg & ~31) != chunk) {
-                  chunk = pg & ~31;
-                  entry = (chunk + lane < a.width) ? row_table[chunk + lane] : 0;
-                }
-                const int row = __shfl_sync(0xffffffffu, entry, pg & 31) * a.page + tok % a.page;
+                const int row = table.page(pg, lane) * a.page + tok % a.page;
                 if (lane == 0) {
                   for (int blk = 0; blk < NB; ++blk) {
                     tma_load_3d(dst + blk * BN * 128 + k * box_bytes, map, &full[st], blk * 64, c.h, row);
