@@ -464,7 +464,8 @@ __global__ void __launch_bounds__(384, 1)
               const bool ready = wait_all_or_fail(pv_t ? &p_half[t] : nullptr, (pbits >> t) & 1,
                                                   (pv_t && !v_seen) ? &v_full[vst] : nullptr, v_par,
                                                   (qk_t && !k_seen) ? &k_full[knext] : nullptr, k_par,
-                                                  (pv_t && j == 0) ? &o_empty[t] : nullptr, ((obits >> t) & 1) ^ 1, 53 + t);
+                                                  (pv_t && j == 0) ? &o_empty[t] : nullptr,
+                                                  ((obits >> t) & 1) ^ 1, 53 + t);
               v_seen = v_seen || pv_t;
               k_seen = k_seen || qk_t;
               if (ready) {

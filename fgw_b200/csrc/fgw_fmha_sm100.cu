@@ -5,12 +5,12 @@
 // mha_paged_decode_ascend_cube_general.py:49-157). B200 design:
 //   * persistent CTAs (<= one per SM) walk work items (request, head, split, 128-row query tile)
 //     round-robin in descending-cache-length order;
-//   * warp 0 issues TMA: the query tile straight from Q[B,Sq,H,D] through a 4-D tensor map (rows past
-//     Sq are zero-filled, so no head-major copy of Q is needed, cf. v7.py:472), and K/V tiles of BN tokens
-//     as one 3-D box per (64-column block, page slice) addressed through the block table;
-//   * warp 1 (one thread) issues tcgen05.mma: S = Q K^T into one of two TMEM buffers, then
-//     O += P V into a TMEM accumulator; QK of tile j+1 is issued before PV of tile j so the tensor
-//     core works while the softmax warps handle tile j;
+//   * warp 0 (converged, lane 0 issuing) runs TMA: the query tile straight from Q[B,Sq,H,D] through a 4-D
+//     tensor map (rows past Sq are zero-filled, so no head-major copy of Q is needed, cf. v7.py:472), and K/V
+//     tiles of BN tokens as one 3-D box per (64-column block, page slice) addressed through the block table;
+//   * warp 1 (converged, one elected lane issuing) runs tcgen05.mma: S = Q K^T into one of two TMEM
+//     buffers, then O += P V into a TMEM accumulator; QK of tile j+1 is issued before PV of tile j so the
+//     tensor core works while the softmax warps handle tile j;
 //   * warps 4..7 own one query row per thread (TMEM lane = row): load the S row, mask tails and the
 //     right-aligned causal diagonal, run the base-2 online softmax, write P (bf16/fp16, 128B-swizzled
 //     K-major) to shared memory, rescale O in TMEM only when the row max grew by more than 2^8, and
